@@ -1,0 +1,437 @@
+"""Benchmark of the elastic sparse attention hot path on B200.
+
+Workload (BASELINE.json metric, configuration C3): forward + backward of the
+8 layers of the elastic pattern P8 (attention_length=64, num_hidden_layers=8,
+layer_idx 0..7) at B=1 per GPU, 32 query heads / 8 KV heads, L=131072,
+head_dim=128, bf16, q/k/v/dO ~ N(0,1) from a seed (synthetic).  One step runs
+the 8 layers on the same inputs.  Inputs (2.5 GB per GPU) are larger than the
+126 MB L2, so no flush is needed between steps.
+
+Metric: effective TFLOP/s over active blocks =
+    sum over layers of 3.5 * 4 * D * 128 * 128 * (#(128-query tile, 128-key
+    block) pairs holding >= 1 valid (query, key) entry, over all heads)
+divided by the time; fwd counts 4*D per pair and bwd 10*D (x3.5 total).
+The line also reports ms/call, useful TFLOP/s (14 * D * valid pairs / time),
+per-kernel times, a roofline for the dominant kernel, the CPU baseline (the
+oracle port of the reference's naive path on a bounded row sample) and an
+end-to-end figure through the public module with host buffers.
+
+Multi-GPU (torchrun): batch split with no collective -- each rank runs its own
+B=1 instance (weak scaling); the time is the max over ranks.
+`--impl reference` times the reference's CPU path (oracle port) instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, HQ, HKV, L, D, W, NL = 1, 32, 8, 131072, 128, 64, 8
+TILE = 128
+METRIC = "effective TFLOP/s (active blocks), fwd+bwd, 128k ctx"
+UNIT = "TFLOP/s"
+WORKLOAD = "C3: fwd+bwd of the 8 P8 layers (w=64, nl=8), B=1/GPU, 32q/8kv heads, L=131072, D=128, bf16"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# Per layer of P8 at L=131072, 32 query heads: active (128-query tile, 128-key
+# block) pairs summed over heads, and valid (head, query, key) entries.  Computed
+# with the C restatement of the pattern (oracle/pattern_ref.c); bench_ours
+# recomputes them from the device pattern kernel and checks they agree.
+ACTIVE_BLOCKS_C3 = [65504, 2368304, 3107986, 3253016, 3250472, 3187795, 3095844, 2985329]
+VALID_PAIRS_C3 = [268370944] * 8
+
+
+def active_blocks_and_pairs(esa, dev):
+    """Per layer: (# active (128-query tile, 128-key block) pairs over heads,
+    # valid (head, query, key) entries), from the device pattern kernel."""
+    out = []
+    nt = (L + TILE - 1) // TILE
+    hh = torch.arange(HQ, device=dev).view(HQ, 1, 1)
+    for layer in range(NL):
+        spec = esa.PatternSpec(layer, NL, W)
+        act = valid = 0
+        rows_blk = 4096
+        for r0 in range(0, L, rows_blk):
+            n = min(rows_blk, L - r0)
+            idx, mask = esa.ops.pattern_indices(HQ, spec, n, dev, row_offset=r0)
+            m = mask.bool()
+            valid += int(m.sum())
+            tile = (torch.arange(r0, r0 + n, device=dev) // TILE).view(1, n, 1)
+            key = ((hh * nt + tile) * nt + idx // TILE)[m]
+            act += int(torch.unique(key).numel())
+            del idx, mask, m, key
+        out.append((act, valid))
+    return out
+
+
+def make_inputs(dev, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(B, HQ, L, D, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, HKV, L, D, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, HKV, L, D, device=dev, generator=g).to(torch.bfloat16)
+    do = torch.randn(B, HQ, L, D, device=dev, generator=g).to(torch.bfloat16)
+    return q, k, v, do
+
+
+def cpu_baseline_sample(target_s: float, layer: int = NL - 1, threads: int | None = None):
+    """The reference's naive path (oracle port) fwd+bwd on bounded samples of
+    query rows of one layer on the host.  The backward is the oracle's hand-
+    written form of the ops autograd runs through the naive path: the
+    reference's own autograd backward of ``take_along_dim`` materialises a
+    [B, H, rows, L, D] gradient (68 GB for 32 rows at L=131072), so it cannot
+    run at this length.  Two sample sizes give the per-row slope and the fixed
+    per-call cost; the step time is extrapolated as NL * (fixed + slope * L).
+    Returns (seconds per step, rows of the larger sample, threads)."""
+    from oracle import naive, pattern
+    nthreads = threads or os.cpu_count() or 1
+    torch.set_num_threads(nthreads)
+    g = torch.Generator().manual_seed(0)
+    k = torch.randn(B, HKV, L, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, HKV, L, D, generator=g).to(torch.bfloat16)
+
+    def run(rows):
+        pos = torch.arange(L - rows, L)   # late rows: the full w keys each
+        q = torch.randn(B, HQ, rows, D, generator=g).to(torch.bfloat16)
+        do = torch.randn(B, HQ, rows, D, generator=g).to(torch.bfloat16)
+        idx, mask, _ = pattern.prepared_indices(HQ, W, layer, NL, L, rows, L, pos.numpy())
+        t0 = time.perf_counter()
+        naive.naive_forward_backward_manual(q, k, v, do, torch.from_numpy(idx),
+                                            torch.from_numpy(mask), D ** -0.5, HQ // HKV,
+                                            chunk=256)
+        return time.perf_counter() - t0
+
+    run(16)
+    r_a = 64
+    t_a = run(r_a)
+    r_b = 256
+    t_b = run(r_b)
+    slope = max((t_b - t_a) / (r_b - r_a), 1e-7)
+    budget = max(0.0, target_s - t_a - t_b)
+    if budget > 2 * t_b:
+        r_c = int(min(L, r_b + budget / slope))
+        r_c = max(r_b + 256, (r_c // 256) * 256)
+        t_c = run(r_c)
+        slope = max((t_c - t_a) / (r_c - r_a), 1e-7)
+        r_b = r_c
+    fixed = max(0.0, t_a - slope * r_a)
+    return NL * (fixed + slope * L), r_b, nthreads
+
+
+def bench_ours(args, world, rank, local):
+    import elastic_sparse_attention_b200 as esa
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    hbm_peak, tc_peak, peak_src = peaks()
+    q, k, v, do = make_inputs(dev, seed=1234 + rank)
+    scale = D ** -0.5
+    specs = [esa.PatternSpec(layer, NL, W) for layer in range(NL)]
+    ws = torch.empty(esa.ops.backward_workspace_bytes(q, k, specs[0]), dtype=torch.uint8, device=dev)
+    for s in specs:   # one-time pattern audit (backward precondition), outside timing
+        assert esa.ops.pattern_audit(HQ, s, L, dev) == 0
+
+    def step():
+        for s in specs:
+            o, lse = esa.ops.forward(q, k, v, s, scale)
+            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+
+    # Per-kernel breakdown (separate pass, events on the launching stream).
+    per_layer = []
+    kern = {"fwd": 0.0, "bwd": 0.0}
+    for s in specs:
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        reps = 2
+        ev[0].record(stream)
+        for _ in range(reps):
+            o, lse = esa.ops.forward(q, k, v, s, scale)
+        ev[1].record(stream)
+        for _ in range(reps):
+            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws)
+        ev[2].record(stream)
+        torch.cuda.synchronize()
+        f_ms, b_ms = ev[0].elapsed_time(ev[1]) / reps, ev[1].elapsed_time(ev[2]) / reps
+        per_layer.append({"layer": s.layer_idx, "fwd_ms": round(f_ms, 3), "bwd_ms": round(b_ms, 3)})
+        kern["fwd"] += f_ms
+        kern["bwd"] += b_ms
+
+    blocks = active_blocks_and_pairs(esa, dev)
+    if [a for a, _ in blocks] != ACTIVE_BLOCKS_C3 or [p for _, p in blocks] != VALID_PAIRS_C3:
+        raise RuntimeError(f"device pattern block counts {blocks} disagree with the oracle table")
+    eff_flop = sum(3.5 * 4 * D * TILE * TILE * a for a, _ in blocks) * B
+    useful_flop = sum(14 * D * p for _, p in blocks) * B
+    value = eff_flop * world / (ms * 1e-3) / 1e12
+    useful = useful_flop * world / (ms * 1e-3) / 1e12
+
+    # Roofline of the dominant kernel family (backward): compulsory HBM bytes
+    # per launch set over its measured time.
+    es = 2
+    q_b, kv_b = B * HQ * L * D * es, B * HKV * L * D * es
+    pairs_total = sum(p for _, p in blocks) / NL
+    bwd_bytes = (3 * q_b + 2 * kv_b + B * HQ * L * 4   # read q, o, dO, k, v, lse
+                 + q_b + 2 * kv_b                      # write dq, dk, dv
+                 + 2 * B * HQ * W * L * 8              # (p, dS) workspace write + read
+                 + 2 * 2 * B * HKV * L * D * 4 * (HQ // HKV - 1))  # fp32 dK/dV accumulators
+    fwd_bytes = q_b + 2 * kv_b + q_b + B * HQ * L * 4
+    dom = "bwd" if kern["bwd"] >= kern["fwd"] else "fwd"
+    dom_ms = kern[dom] / NL
+    dom_bytes = bwd_bytes if dom == "bwd" else fwd_bytes
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get(dom)
+        except Exception:
+            traffic = None
+    roofline = {"bound": "hbm", "kernel": f"{dom} (per layer, all launches)",
+                "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                "peak_source": peak_src,
+                "gather_GBps": round(2 * 2 * pairs_total * D * es * (2 if dom == "bwd" else 1)
+                                     / (dom_ms * 1e-3) / 1e9, 1),
+                "note": "algorithmic = compulsory HBM bytes; the gather kernels are bound by "
+                        "L1/L2->SM row-gather bandwidth (gather_GBps), not HBM"}
+
+    # End to end through the public module with pinned host buffers.
+    e2e = e2e_module(esa, args, dev, world)
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic N(0,1), seeded",
+        "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": L,
+                   "heads": f"{HQ}q/{HKV}kv", "head_dim": D, "attention_length": W,
+                   "num_hidden_layers": NL, "parallelism": f"batch split x{world}, no collective",
+                   "l2": "inputs 2.5 GB/GPU > 126 MB L2, no flush"},
+        "useful_tflops": round(useful, 2),
+        "useful_frac_of_bf16_peak": round(useful / tc_peak, 5),
+        "effective_frac_of_bf16_peak": round(value / world / tc_peak, 4),
+        "kernel_ms_per_step": {k2: round(v2, 3) for k2, v2 in kern.items()},
+        "per_layer": per_layer,
+        "active_blocks_per_layer": [a for a, _ in blocks],
+        "roofline": roofline,
+        "gpu_launches": args.steps * NL * (2 + HQ // HKV),
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        sec_step, rows, thr = cpu_baseline_sample(args.cpu_seconds)
+        line["cpu_baseline"] = {
+            "value": round(eff_flop / sec_step / 1e12, 6), "unit": UNIT, "cores": thr,
+            "kind": "port",
+            "sample": f"oracle port of the reference naive path (bf16, torch CPU), fwd+bwd, "
+                      f"layer {NL - 1}, last {rows} query rows x {HQ} heads, extrapolated "
+                      f"linearly to {L} rows x {NL} layers ({sec_step:.1f} s/step)"}
+    return line
+
+
+def e2e_module(esa, args, dev, world):
+    """The same step through ElasticSparseAttention + autograd, with q/k/v/dO
+    copied from pinned host memory each step and dq/dk/dv read back."""
+    g = torch.Generator().manual_seed(99)
+    hq = torch.randn(B, HQ, L, D, generator=g).to(torch.bfloat16).pin_memory()
+    hk = torch.randn(B, HKV, L, D, generator=g).to(torch.bfloat16).pin_memory()
+    hv = torch.randn(B, HKV, L, D, generator=g).to(torch.bfloat16).pin_memory()
+    hdo = torch.randn(B, L, HQ * D, generator=g).to(torch.bfloat16).pin_memory()
+    outs = [torch.empty(B, HQ, L, D, dtype=torch.bfloat16).pin_memory(),
+            torch.empty(B, HKV, L, D, dtype=torch.bfloat16).pin_memory(),
+            torch.empty(B, HKV, L, D, dtype=torch.bfloat16).pin_memory()]
+    mods = [esa.ElasticSparseAttention(layer, NL, HQ, D, W, L, num_key_value_heads=HKV)
+            for layer in range(NL)]
+
+    def step():
+        q = hq.to(dev, non_blocking=True).requires_grad_(True)
+        k = hk.to(dev, non_blocking=True).requires_grad_(True)
+        v = hv.to(dev, non_blocking=True).requires_grad_(True)
+        do = hdo.to(dev, non_blocking=True)
+        for m in mods:
+            out, _ = m(q, k, v)
+            out.backward(do)
+        for h, t in zip(outs, (q.grad, k.grad, v.grad)):
+            h.copy_(t, non_blocking=True)
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    n = max(1, min(args.steps, 3))
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(n):
+        step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    blocks_flop = getattr(e2e_module, "_eff_flop", None)
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
+    d2h = sum(t.numel() * t.element_size() for t in outs)
+    return {"ms_per_step": round(ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "unit": UNIT, "value": None, "_flop_ref": blocks_flop, "steps": n}
+
+
+def bench_reference(args, world, rank):
+    """CPU reference arm: the reference naive path (oracle port) on host cores."""
+    if rank != 0:
+        return None
+    per_step_budget = max(2.0, 150.0 / max(1, args.steps + args.warmup))
+    sec_step, rows, thr = cpu_baseline_sample(per_step_budget)
+    eff = sum(3.5 * 4 * D * TILE * TILE * a for a in ACTIVE_BLOCKS_C3)
+    value = eff * B / sec_step / 1e12
+    return {"metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec_step * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1), seeded", "impl": "reference",
+            "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": L,
+                       "parallelism": "host CPU, rank 0 only"},
+            "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": thr, "kind": "port",
+                             "sample": f"layer {NL - 1}, last {rows} query rows x {HQ} heads per "
+                                       "step, extrapolated linearly in rows and layers"},
+            "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = bench_reference(args, world, rank)
+        if line:
+            print(json.dumps(line), flush=True)
+        return
+    world, rank, local = dist_init()
+    line = bench_ours(args, world, rank, local)
+    if rank == 0:
+        eff_per_step = line["value"] * line["ms_per_step"] * 1e-3 * 1e12
+        e2e = line["e2e"]
+        e2e["value"] = round(eff_per_step / (e2e["ms_per_step"] * 1e-3) / 1e12, 2)
+        e2e.pop("_flop_ref", None)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

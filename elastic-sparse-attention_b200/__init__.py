@@ -1,0 +1,14 @@
+"""B200-native elastic sparse attention (sm_100a CUDA kernels behind a C ABI).
+
+Drop-in for ``elastic_sparse_attention.ElasticSparseAttention`` of
+HighCWu/elastic-sparse-attention.  Import it as ``elastic_sparse_attention_b200``
+(the loader module of that name at the repository root maps it to this
+directory).
+"""
+from . import _lib, ops
+from .attention import ElasticSparseAttention, ElasticSparseAttentionFunction
+from .ops import PatternSpec
+
+__all__ = ["ElasticSparseAttention", "ElasticSparseAttentionFunction", "PatternSpec", "ops",
+           "_lib"]
+__version__ = "0.1.0"

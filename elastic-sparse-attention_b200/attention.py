@@ -1,0 +1,230 @@
+"""Drop-in ``ElasticSparseAttention`` module backed by hand-written sm_100a kernels.
+
+Mirrors ``elastic_sparse_attention.py:345-765`` of HighCWu/elastic-sparse-attention:
+the same constructor arguments and validation errors, the same
+``forward(query_states, key_states, value_states, cache_position=None)``
+signature and the same ``(attn_output [B, q_len, H*D], attn_weights)`` result.
+
+Differences, all deliberate:
+
+* Every ``implementation`` value ("triton", "naive", "dense") is accepted and
+  validated as in the reference (:412-417) but runs the same CUDA path; there
+  is no Triton, no PyTorch fallback and no CPU path.  ``attn_weights`` is
+  ``None`` (as the reference's triton and dense paths return, :622, :726).
+* The pattern is computed inside the kernels from (position, head, slot), so
+  nothing of size ``[H, max_seq_len, w]`` is built at construction (the
+  reference builds it on the CPU, :454-468).  ``sparse_attention_indices``,
+  ``sparse_causal_mask`` and ``full_attention_mask`` are still available, built
+  lazily on the GPU on first access, bit-exact with the reference buffers.
+* ``attention_dropout`` is stored but not applied, like the reference's triton
+  path (which has no dropout); a one-time warning says so when it is > 0.
+"""
+from __future__ import annotations
+
+import logging
+import threading
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from . import ops
+from .ops import PatternSpec
+
+logger = logging.getLogger(__name__)
+
+_audit_lock = threading.Lock()
+_audited: dict[tuple, int] = {}   # (H, w, layer, nl) -> longest audited sequence length
+
+
+def _ensure_monotone(num_heads: int, spec: PatternSpec, seq_len: int, device: torch.device):
+    """The backward's key-side enumeration needs every per-slot index column to
+    be non-decreasing along positions; check it once per pattern and length."""
+    key = (num_heads, spec.attention_length, spec.layer_idx, spec.num_hidden_layers)
+    with _audit_lock:
+        if _audited.get(key, 0) >= seq_len:
+            return
+    bad = ops.pattern_audit(num_heads, spec, seq_len, device)
+    if bad:
+        raise RuntimeError(
+            f"elastic pattern {key} has {bad} decreasing index steps up to length {seq_len}; "
+            "the backward kernel's transposed enumeration does not support it")
+    with _audit_lock:
+        _audited[key] = max(_audited.get(key, 0), seq_len)
+
+
+class ElasticSparseAttentionFunction(torch.autograd.Function):
+    """Autograd boundary (reference ``ElasticSparseAttentionFunction``, :235-339).
+
+    ``apply(q, k, v, pattern, sm_scale, num_kv_groups, rows=None)``: instead of
+    materialised ``sparse_indices`` / ``sparse_mask`` tensors, ``pattern`` is the
+    :class:`PatternSpec` they are generated from and ``rows`` the optional query
+    positions (``cache_position``).  Returns o ``[B, H, q_len, D]``.
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, pattern: PatternSpec, sm_scale: float, num_kv_groups: int,
+                rows: Optional[torch.Tensor] = None):
+        if q.shape[1] != k.shape[1] * num_kv_groups:
+            raise ValueError("num_kv_groups does not match the query / key head counts")
+        q, k, v = (ops.as_kernel_operand(t) for t in (q, k, v))
+        o, lse = ops.forward(q, k, v, pattern, sm_scale, rows=rows)
+        ctx.save_for_backward(q, k, v, o, lse, rows)
+        ctx.pattern = pattern
+        ctx.sm_scale = sm_scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse, rows = ctx.saved_tensors
+        do = ops.as_kernel_operand(do)
+        spec = ctx.pattern
+        sorted_rows = perm = None
+        if rows is not None:
+            sorted_rows, perm = torch.sort(rows, stable=True)
+            seq = int(sorted_rows[-1].item()) + 1 if rows.numel() else 0
+        else:
+            seq = q.shape[2]
+        _ensure_monotone(q.shape[1], spec, max(seq, 2), q.device)
+        dq, dk, dv = ops.backward(q, k, v, o, lse, do, spec, ctx.sm_scale, rows=rows,
+                                  sorted_rows=sorted_rows, row_perm=perm)
+        return dq, dk, dv, None, None, None, None
+
+
+class ElasticSparseAttention(nn.Module):
+    """Elastic sparse attention with GQA; see the module docstring for the contract.
+
+    Args follow the reference (:375-386): ``layer_idx``, ``num_hidden_layers``,
+    ``num_attention_heads``, ``head_dim``, ``attention_length`` (w),
+    ``max_seq_len``, ``num_key_value_heads=None`` (MHA), ``attention_dropout=0.0``,
+    ``implementation="triton"``.
+    """
+
+    def __init__(self, layer_idx: int, num_hidden_layers: int, num_attention_heads: int,
+                 head_dim: int, attention_length: int, max_seq_len: int,
+                 num_key_value_heads: Optional[int] = None, attention_dropout: float = 0.0,
+                 implementation: str = "triton"):
+        super().__init__()
+        valid_implementations = ["triton", "naive", "dense"]
+        if implementation not in valid_implementations:
+            raise ValueError(
+                f"Invalid implementation '{implementation}'. Must be one of "
+                f"{valid_implementations}.")
+        self.layer_idx = layer_idx
+        self.num_hidden_layers = num_hidden_layers
+        self.num_attention_heads = num_attention_heads
+        self.head_dim = head_dim
+        self.attention_length = attention_length
+        self.attention_dropout = attention_dropout
+        self.implementation = implementation
+        self.max_seq_len = max_seq_len
+        self.num_key_value_heads = (num_key_value_heads if num_key_value_heads is not None
+                                    else num_attention_heads)
+        if self.num_attention_heads % self.num_key_value_heads != 0:
+            raise ValueError(
+                f"`num_attention_heads` ({self.num_attention_heads}) must be divisible by "
+                f"`num_key_value_heads` ({self.num_key_value_heads}) for GQA.")
+        self.num_kv_groups = self.num_attention_heads // self.num_key_value_heads
+        self.scaling = self.head_dim ** -0.5
+        if max_seq_len > ops.MAX_POSITION:
+            raise ValueError(f"max_seq_len ({max_seq_len}) above {ops.MAX_POSITION} is not "
+                             "supported (float32 position arithmetic)")
+        if attention_dropout > 0:
+            logger.warning("attention_dropout=%s is not applied (as in the reference's triton "
+                           "path)", attention_dropout)
+        self.pattern = PatternSpec(layer_idx, num_hidden_layers, attention_length)
+        self._buffers_cache: dict = {}
+
+    # -- pattern buffers (lazy; reference :446-468) --------------------------
+    def _pattern_device(self) -> torch.device:
+        if not torch.cuda.is_available():
+            raise RuntimeError("pattern buffers are built by a CUDA kernel; no GPU is visible")
+        return torch.device("cuda", torch.cuda.current_device())
+
+    def _create_elastic_sparse_indices(self, seq_len: int, device=None):
+        """(indices, mask) int64 [H, seq_len, w], reference :470-535 (built on the GPU)."""
+        dev = self._pattern_device() if device is None else torch.device(device)
+        return ops.pattern_indices(self.num_attention_heads, self.pattern, seq_len, dev)
+
+    def _cached_pattern(self):
+        dev = self._pattern_device()
+        key = ("sparse", dev)
+        if key not in self._buffers_cache:
+            self._buffers_cache[key] = self._create_elastic_sparse_indices(self.max_seq_len, dev)
+        return self._buffers_cache[key]
+
+    @property
+    def sparse_attention_indices(self) -> torch.Tensor:
+        return self._cached_pattern()[0]
+
+    @property
+    def sparse_causal_mask(self) -> torch.Tensor:
+        return self._cached_pattern()[1]
+
+    @property
+    def full_attention_mask(self) -> torch.Tensor:
+        """Dense bool [1, H, L, L] mask (reference :537-572); O(L^2) memory."""
+        dev = self._pattern_device()
+        key = ("full", dev)
+        if key not in self._buffers_cache:
+            L = self.max_seq_len
+            idx, mask = self._cached_pattern()
+            full = torch.zeros(self.num_attention_heads, L, L, dtype=torch.bool, device=dev)
+            h = torch.arange(self.num_attention_heads, device=dev).view(-1, 1, 1).expand_as(idx)
+            qpos = torch.arange(L, device=dev).view(1, -1, 1).expand_as(idx)
+            m = mask.bool()
+            full[h[m], qpos[m], idx.clamp(0, L - 1)[m]] = True
+            self._buffers_cache[key] = full.unsqueeze(0)
+        return self._buffers_cache[key]
+
+    def _get_prepared_indices_and_mask(self, kv_seq_len: int):
+        """Slices of the pattern buffers for ``kv_seq_len`` (reference :574-590)."""
+        if kv_seq_len > self.max_seq_len:
+            raise ValueError(
+                f"Input sequence length ({kv_seq_len}) exceeds the maximum length initialized "
+                f"in the module ({self.max_seq_len}).")
+        return self.sparse_attention_indices[:, :kv_seq_len, :], \
+            self.sparse_causal_mask[:, :kv_seq_len, :]
+
+    # -- forward (reference :728-765) ----------------------------------------
+    def forward(self, query_states: torch.Tensor, key_states: torch.Tensor,
+                value_states: torch.Tensor, cache_position: Optional[torch.LongTensor] = None,
+                ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+        q_seq_len = query_states.shape[2]
+        kv_seq_len = key_states.shape[2]
+        if kv_seq_len > self.max_seq_len:
+            raise ValueError(
+                f"Input sequence length ({kv_seq_len}) exceeds the maximum length initialized "
+                f"in the module ({self.max_seq_len}).")
+        rows = None
+        if cache_position is not None:
+            rows = self._prepare_rows(cache_position, q_seq_len, kv_seq_len,
+                                      query_states.device)
+        elif q_seq_len > kv_seq_len:
+            raise ValueError(f"q_len ({q_seq_len}) > kv_len ({kv_seq_len}) needs cache_position")
+        attn_output = ElasticSparseAttentionFunction.apply(
+            query_states, key_states, value_states, self.pattern, self.scaling,
+            self.num_kv_groups, rows)
+        batch_size, _, q_len, head_dim = query_states.shape
+        hidden_dim = self.num_attention_heads * head_dim
+        attn_output = attn_output.transpose(1, 2).reshape(batch_size, q_len, hidden_dim)
+        return attn_output, None
+
+    @staticmethod
+    def _prepare_rows(cache_position, q_seq_len: int, kv_seq_len: int, device) -> torch.Tensor:
+        """Query positions for ``cache_position`` as the reference indexes the
+        ``[:kv_len]`` slice of its buffers (:607-608): negative entries wrap,
+        out-of-range entries raise IndexError."""
+        rows = torch.as_tensor(cache_position, device=device).to(torch.int64).reshape(-1)
+        if rows.numel() != q_seq_len:
+            raise ValueError(f"cache_position has {rows.numel()} entries for q_len {q_seq_len}")
+        rows = torch.where(rows < 0, rows + kv_seq_len, rows)
+        if rows.numel() and (int(rows.min()) < 0 or int(rows.max()) >= kv_seq_len):
+            raise IndexError(f"cache_position out of range for kv_len {kv_seq_len}")
+        return rows.contiguous()
+
+    def extra_repr(self) -> str:
+        return (f"layer_idx={self.layer_idx}, num_hidden_layers={self.num_hidden_layers}, "
+                f"heads={self.num_attention_heads}/{self.num_key_value_heads}, "
+                f"head_dim={self.head_dim}, attention_length={self.attention_length}, "
+                f"max_seq_len={self.max_seq_len}")

@@ -1,0 +1,344 @@
+// extern "C" entry points of libesa_b200.so (declared in include/esa_b200.h).
+//
+// Host-side validation, workspace layout, kernel selection and launch.  No
+// entry point allocates device memory: outputs and workspace come from the
+// caller (the Python module takes them from torch's caching allocator).
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "esa_b200.h"
+#include "esa_gather.cuh"
+#include "esa_pattern.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(ESA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return ESA_OK;
+}
+
+constexpr int64_t kMaxPosition = int64_t(1) << 24;  // float32 index math is exact below 2^24
+constexpr int kMaxAttnLength = 2048;
+
+esa::Pattern make_pattern(int num_heads, int w, int layer_idx, int num_hidden_layers) {
+  esa::Pattern P;
+  const int denominator = num_hidden_layers > 1 ? num_hidden_layers - 1 : 1;   // :488
+  const double alpha = (double)layer_idx / (double)denominator;                // :489
+  P.w = w;
+  P.num_heads = num_heads;
+  P.a = (float)alpha;
+  P.c = (float)((double)w * (1.0 - alpha));                                    // :496
+  P.inv_hm1 = 0.f;
+  return P;
+}
+
+int elem_size(int dtype) { return dtype == ESA_DTYPE_F32 ? 4 : 2; }
+
+bool head_dim_supported(int dtype, int d) {
+  if (dtype == ESA_DTYPE_F32) return d == 32 || d == 64 || d == 128;
+  return d == 32 || d == 64 || d == 128 || d == 256;
+}
+
+int check_tensor(const char* name, const esa_tensor_t& t, int esize) {
+  if (!t.data) return fail(ESA_ERR_INVALID, "%s: null data pointer", name);
+  if (reinterpret_cast<uintptr_t>(t.data) % 16)
+    return fail(ESA_ERR_INVALID, "%s: data pointer must be 16-byte aligned", name);
+  if ((t.stride_b * esize) % 16 || (t.stride_h * esize) % 16 || (t.stride_s * esize) % 16)
+    return fail(ESA_ERR_INVALID,
+                "%s: strides (%lld, %lld, %lld) elements must be multiples of 16 bytes",
+                name, (long long)t.stride_b, (long long)t.stride_h, (long long)t.stride_s);
+  return ESA_OK;
+}
+
+int check_problem(const esa_problem_t* pb) {
+  if (!pb) return fail(ESA_ERR_INVALID, "null problem");
+  if (pb->dtype < 0 || pb->dtype > 2) return fail(ESA_ERR_INVALID, "unknown dtype %d", pb->dtype);
+  if (pb->batch < 0 || pb->num_heads < 1 || pb->num_kv_heads < 1)
+    return fail(ESA_ERR_INVALID, "batch/num_heads/num_kv_heads out of range");
+  if (pb->num_heads % pb->num_kv_heads)
+    return fail(ESA_ERR_INVALID, "num_heads (%d) must be divisible by num_kv_heads (%d)",
+                pb->num_heads, pb->num_kv_heads);
+  if (!head_dim_supported(pb->dtype, pb->head_dim))
+    return fail(ESA_ERR_UNSUPPORTED, "head_dim %d not supported for dtype %d", pb->head_dim,
+                pb->dtype);
+  if (pb->attn_length < 1 || pb->attn_length > kMaxAttnLength)
+    return fail(ESA_ERR_UNSUPPORTED, "attention_length %d outside [1, %d]", pb->attn_length,
+                kMaxAttnLength);
+  if (pb->num_hidden_layers < 1) return fail(ESA_ERR_INVALID, "num_hidden_layers must be >= 1");
+  if (pb->q_len < 0 || pb->q_len >= kMaxPosition)
+    return fail(ESA_ERR_INVALID, "q_len %lld out of range", (long long)pb->q_len);
+  if (pb->q_len > 0 && pb->kv_len < 1) return fail(ESA_ERR_INVALID, "kv_len must be >= 1");
+  if (pb->kv_len > kMaxPosition)
+    return fail(ESA_ERR_UNSUPPORTED, "kv_len %lld above 2^24", (long long)pb->kv_len);
+  if (pb->kv_offset < 0 || pb->kv_rows < 1 || pb->kv_offset + pb->kv_rows > kMaxPosition)
+    return fail(ESA_ERR_INVALID, "kv_offset/kv_rows out of range");
+  if (pb->row_offset < 0 || pb->row_offset + pb->q_len > kMaxPosition)
+    return fail(ESA_ERR_INVALID, "row_offset out of range");
+  if (!std::isfinite(pb->scale)) return fail(ESA_ERR_INVALID, "scale must be finite");
+  return ESA_OK;
+}
+
+esa::AttnParams base_params(const esa_problem_t* pb) {
+  esa::AttnParams p{};
+  p.B = pb->batch;
+  p.Hq = pb->num_heads;
+  p.Hkv = pb->num_kv_heads;
+  p.G = pb->num_heads / pb->num_kv_heads;
+  p.D = pb->head_dim;
+  p.n_rows = (int)pb->q_len;
+  p.kv_len = (int)pb->kv_len;
+  p.kv_offset = (int)pb->kv_offset;
+  p.kv_rows = (int)pb->kv_rows;
+  p.row_offset = (int)pb->row_offset;
+  p.rows = pb->rows;
+  p.pat = make_pattern(pb->num_heads, pb->attn_length, pb->layer_idx, pb->num_hidden_layers);
+  p.scale = pb->scale;
+  p.scale_log2 = pb->scale * esa::kLog2e;
+  return p;
+}
+
+void set_tensor(const esa_tensor_t& t, const void*& ptr, int64_t& sb, int64_t& sh, int64_t& ss) {
+  ptr = t.data; sb = t.stride_b; sh = t.stride_h; ss = t.stride_s;
+}
+void set_tensor_mut(const esa_tensor_t& t, void*& ptr, int64_t& sb, int64_t& sh, int64_t& ss) {
+  ptr = t.data; sb = t.stride_b; sh = t.stride_h; ss = t.stride_s;
+}
+
+constexpr int kFwdWarps = 8;
+constexpr int kKeyWarps = 8;
+constexpr int kKeyRowsPerWarp = 16;
+
+int rows_per_cta(int G) { return G >= 64 ? 1 : 64 / G; }
+
+template <typename K>
+int prepare_smem(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+        cudaSuccess)
+      return fail(ESA_ERR_CUDA, "cannot reserve %zu bytes of shared memory", bytes);
+  }
+  return ESA_OK;
+}
+
+template <typename T, int D>
+int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
+  const int rpc = rows_per_cta(p.G);
+  const int wpad = (p.pat.w + 31) & ~31;
+  const size_t smem = (size_t)kFwdWarps * 2 * wpad * sizeof(int);
+  auto kern = esa::fwd_gather_kernel<T, D, kFwdWarps>;
+  if (int rc = prepare_smem(kern, smem)) return rc;
+  dim3 grid((p.n_rows + rpc - 1) / rpc, p.Hkv, p.B);
+  kern<<<grid, kFwdWarps * 32, smem, s>>>(p, rpc);
+  return check_launch("forward");
+}
+
+template <typename T, int D>
+int launch_backward(const esa::AttnParams& p, cudaStream_t s) {
+  if (p.n_rows > 0) {
+    const int rpc = rows_per_cta(p.G);
+    const int wpad = (p.pat.w + 31) & ~31;
+    const size_t smem = (size_t)kFwdWarps * 2 * wpad * sizeof(int);
+    auto kern = esa::bwd_query_kernel<T, D, kFwdWarps>;
+    if (int rc = prepare_smem(kern, smem)) return rc;
+    dim3 grid((p.n_rows + rpc - 1) / rpc, p.Hkv, p.B);
+    kern<<<grid, kFwdWarps * 32, smem, s>>>(p, rpc);
+    if (int rc = check_launch("backward (query side)")) return rc;
+  }
+  {
+    const int ncol = (p.pat.w + 31) >> 5;
+    const size_t smem = (size_t)kKeyWarps * ncol * 32 * sizeof(int);
+    auto kern = esa::bwd_key_kernel<T, D, kKeyWarps, kKeyRowsPerWarp>;
+    if (int rc = prepare_smem(kern, smem)) return rc;
+    const int tile = kKeyWarps * kKeyRowsPerWarp;
+    dim3 grid((p.kv_rows + tile - 1) / tile, p.Hkv, p.B);
+    for (int gi = 0; gi < p.G; ++gi) {
+      esa::AttnParams pk = p;
+      pk.head_in_group = gi;
+      kern<<<grid, kKeyWarps * 32, smem, s>>>(pk);
+      if (int rc = check_launch("backward (key side)")) return rc;
+    }
+  }
+  return ESA_OK;
+}
+
+struct FwdOp {
+  template <typename T, int D>
+  static int run(const esa::AttnParams& p, cudaStream_t s) { return launch_forward<T, D>(p, s); }
+};
+struct BwdOp {
+  template <typename T, int D>
+  static int run(const esa::AttnParams& p, cudaStream_t s) { return launch_backward<T, D>(p, s); }
+};
+
+template <typename Op>
+int dispatch_op(int dtype, int d, const esa::AttnParams& p, cudaStream_t s) {
+  switch (dtype) {
+    case ESA_DTYPE_F32:
+      switch (d) {
+        case 32: return Op::template run<float, 32>(p, s);
+        case 64: return Op::template run<float, 64>(p, s);
+        case 128: return Op::template run<float, 128>(p, s);
+      }
+      break;
+    case ESA_DTYPE_BF16:
+      switch (d) {
+        case 32: return Op::template run<__nv_bfloat16, 32>(p, s);
+        case 64: return Op::template run<__nv_bfloat16, 64>(p, s);
+        case 128: return Op::template run<__nv_bfloat16, 128>(p, s);
+        case 256: return Op::template run<__nv_bfloat16, 256>(p, s);
+      }
+      break;
+    case ESA_DTYPE_F16:
+      switch (d) {
+        case 32: return Op::template run<__half, 32>(p, s);
+        case 64: return Op::template run<__half, 64>(p, s);
+        case 128: return Op::template run<__half, 128>(p, s);
+        case 256: return Op::template run<__half, 256>(p, s);
+      }
+      break;
+  }
+  return fail(ESA_ERR_UNSUPPORTED, "dtype %d with head_dim %d not built", dtype, d);
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+size_t pds_bytes(const esa_problem_t* pb) {
+  return align256((size_t)pb->batch * pb->num_heads * pb->attn_length * pb->q_len * sizeof(float2));
+}
+size_t acc_bytes(const esa_problem_t* pb) {
+  if (pb->num_heads == pb->num_kv_heads) return 0;
+  return align256((size_t)2 * pb->batch * pb->num_kv_heads * pb->kv_rows * pb->head_dim *
+                  sizeof(float));
+}
+
+}  // namespace
+
+extern "C" {
+
+int esa_version(void) { return 100; }
+
+const char* esa_last_error(void) { return g_last_error.c_str(); }
+
+int esa_pattern(int32_t num_heads, int32_t attn_length, int32_t layer_idx,
+                int32_t num_hidden_layers, int64_t n_rows, const int64_t* rows,
+                int64_t row_offset, int64_t clamp_len, int64_t* idx, int64_t* mask,
+                void* stream) {
+  if (num_heads < 1 || attn_length < 1 || attn_length > kMaxAttnLength || num_hidden_layers < 1)
+    return fail(ESA_ERR_INVALID, "esa_pattern: bad pattern arguments");
+  if (n_rows < 0 || row_offset < 0 || row_offset + n_rows > kMaxPosition ||
+      clamp_len > kMaxPosition)
+    return fail(ESA_ERR_INVALID, "esa_pattern: rows out of range (positions must be < 2^24)");
+  if (n_rows == 0) return ESA_OK;
+  if (!idx || !mask) return fail(ESA_ERR_INVALID, "esa_pattern: null output");
+  const esa::Pattern P = make_pattern(num_heads, attn_length, layer_idx, num_hidden_layers);
+  const int64_t total = (int64_t)num_heads * n_rows * attn_length;
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 64);
+  esa::pattern_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
+      P, (int)n_rows, rows, (int)row_offset, (int)(clamp_len > 0 ? clamp_len : 0), idx, mask);
+  return check_launch("esa_pattern");
+}
+
+int esa_pattern_audit(int32_t num_heads, int32_t attn_length, int32_t layer_idx,
+                      int32_t num_hidden_layers, int64_t seq_len, unsigned long long* d_count,
+                      void* stream) {
+  if (num_heads < 1 || attn_length < 1 || attn_length > kMaxAttnLength || num_hidden_layers < 1 ||
+      seq_len < 0 || seq_len > kMaxPosition || !d_count)
+    return fail(ESA_ERR_INVALID, "esa_pattern_audit: bad arguments");
+  if (seq_len < 2) return ESA_OK;
+  const esa::Pattern P = make_pattern(num_heads, attn_length, layer_idx, num_hidden_layers);
+  const int64_t total = (int64_t)num_heads * seq_len * attn_length;
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 32);
+  esa::audit_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(P, (int)seq_len,
+                                                                            d_count);
+  return check_launch("esa_pattern_audit");
+}
+
+int esa_forward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_tensor_t v,
+                esa_tensor_t o, float* lse, void* stream) {
+  if (int rc = check_problem(pb)) return rc;
+  if (pb->q_len == 0 || pb->batch == 0) return ESA_OK;
+  const int es = elem_size(pb->dtype);
+  if (int rc = check_tensor("q", q, es)) return rc;
+  if (int rc = check_tensor("k", k, es)) return rc;
+  if (int rc = check_tensor("v", v, es)) return rc;
+  if (int rc = check_tensor("o", o, es)) return rc;
+  if (!lse) return fail(ESA_ERR_INVALID, "lse: null pointer");
+  esa::AttnParams p = base_params(pb);
+  set_tensor(q, p.q, p.sqb, p.sqh, p.sqs);
+  set_tensor(k, p.k, p.skb, p.skh, p.sks);
+  set_tensor(v, p.v, p.svb, p.svh, p.svs);
+  set_tensor_mut(o, p.o, p.sob, p.soh, p.sos);
+  p.lse = lse;
+  return dispatch_op<FwdOp>(pb->dtype, pb->head_dim, p, (cudaStream_t)stream);
+}
+
+size_t esa_backward_workspace_size(const esa_problem_t* pb) {
+  if (!pb || pb->batch < 0 || pb->q_len < 0 || pb->attn_length < 0) return 0;
+  return pds_bytes(pb) + acc_bytes(pb);
+}
+
+int esa_backward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_tensor_t v,
+                 esa_tensor_t o, const float* lse, esa_tensor_t dout, esa_tensor_t dq,
+                 esa_tensor_t dk, esa_tensor_t dv, const int64_t* sorted_rows,
+                 const int64_t* row_perm, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  if (int rc = check_problem(pb)) return rc;
+  if (pb->batch == 0) return ESA_OK;
+  const int es = elem_size(pb->dtype);
+  if (int rc = check_tensor("k", k, es)) return rc;
+  if (int rc = check_tensor("v", v, es)) return rc;
+  if (int rc = check_tensor("dk", dk, es)) return rc;
+  if (int rc = check_tensor("dv", dv, es)) return rc;
+  if (pb->q_len > 0) {
+    if (int rc = check_tensor("q", q, es)) return rc;
+    if (int rc = check_tensor("o", o, es)) return rc;
+    if (int rc = check_tensor("dout", dout, es)) return rc;
+    if (int rc = check_tensor("dq", dq, es)) return rc;
+    if (!lse) return fail(ESA_ERR_INVALID, "lse: null pointer");
+  }
+  if ((sorted_rows == nullptr) != (row_perm == nullptr))
+    return fail(ESA_ERR_INVALID, "sorted_rows and row_perm must be given together");
+  const size_t need = esa_backward_workspace_size(pb);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(ESA_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes,
+                need);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(ESA_ERR_INVALID, "workspace must be 256-byte aligned");
+  esa::AttnParams p = base_params(pb);
+  set_tensor(q, p.q, p.sqb, p.sqh, p.sqs);
+  set_tensor(k, p.k, p.skb, p.skh, p.sks);
+  set_tensor(v, p.v, p.svb, p.svh, p.svs);
+  set_tensor_mut(o, p.o, p.sob, p.soh, p.sos);
+  set_tensor(dout, p.dout, p.sdob, p.sdoh, p.sdos);
+  set_tensor_mut(dq, p.dq, p.sdqb, p.sdqh, p.sdqs);
+  set_tensor_mut(dk, p.dk, p.sdkb, p.sdkh, p.sdks);
+  set_tensor_mut(dv, p.dv, p.sdvb, p.sdvh, p.sdvs);
+  p.lse = const_cast<float*>(lse);
+  p.sorted_rows = sorted_rows;
+  p.row_perm = row_perm;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  p.pds = reinterpret_cast<float2*>(ws);
+  p.acc = acc_bytes(pb) ? reinterpret_cast<float*>(ws + pds_bytes(pb)) : nullptr;
+  return dispatch_op<BwdOp>(pb->dtype, pb->head_dim, p, (cudaStream_t)stream);
+}
+
+}  // extern "C"

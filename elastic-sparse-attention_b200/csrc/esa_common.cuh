@@ -1,0 +1,177 @@
+// Shared device code for the elastic sparse attention kernels (sm_100a).
+//
+// Index math: bit-exact restatement of the reference's pattern generator
+// (elastic_sparse_attention.py:470-535).  torch evaluates that function in
+// float32 with one rounding per operation and rounds half to even; the device
+// code does the same with __fmul_rn / __fadd_rn / __fsub_rn / __fdiv_rn (never
+// contracted into an FMA) and rintf (round to nearest even).  All integer <->
+// float conversions are exact because positions are below 2^24 (checked by the
+// host entry points).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace esa {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Per-layer constants of the pattern (reference :476-499).
+struct Pattern {
+  int w;          // attention_length
+  int num_heads;  // query heads H (the pattern is defined per query head)
+  float a;        // f32(alpha), alpha = layer_idx / max(nl - 1, 1)          :488-489
+  float c;        // f32(w * (1 - alpha)), the product taken in double        :496
+  float inv_hm1;  // unused by the bit-exact path; kept 0
+};
+
+// Start and spacing of the window of one query position (reference :482-499).
+struct RowWin {
+  int st;    // start_ids_base                                                :497
+  float sp;  // spacing_base                                                  :498-499
+};
+
+__device__ __forceinline__ RowWin row_window(const Pattern& P, int pos) {
+  const int end = pos > P.w - 1 ? pos : P.w - 1;                            // :483
+  const float E = __int2float_rn(end + 1);                                  // :495
+  const float pd = __fadd_rn(P.c, __fmul_rn(E, P.a));                       // :496
+  float s = rintf(__fsub_rn(E, pd));                                        // :497 round
+  s = s < 0.f ? 0.f : s;                                                    // :497 clamp
+  RowWin r;
+  r.st = __float2int_rz(s);
+  r.sp = __fdiv_rn(__int2float_rn(end + 1 - r.st), __int2float_rn(P.w));    // :498-499
+  return r;
+}
+
+// attention_indices_oversized[:, k] (reference :503-506)
+__device__ __forceinline__ int oversized(const RowWin& r, int k) {
+  return r.st + __float2int_rz(rintf(__fmul_rn(__int2float_rn(k), r.sp)));
+}
+
+// Head interpolation weight t = h / (H - 1) (reference :515-516).
+__device__ __forceinline__ float head_weight(const Pattern& P, int h) {
+  return P.num_heads > 1 ? __fdiv_rn(__int2float_rn(h), __int2float_rn(P.num_heads - 1)) : 0.f;
+}
+
+// Raw (unmasked, unclamped) index of slot k for a head with weight t:
+// round(base * (1 - t) + shifted * t) with base = ov[k], shifted = ov[k+1] - 1
+// (reference :510-511, :521-526).
+__device__ __forceinline__ int raw_index(const RowWin& r, int k, float t, float omt) {
+  const int ov0 = oversized(r, k);
+  const int ov1 = oversized(r, k + 1);
+  const float x = __fmul_rn(__int2float_rn(ov0), omt);
+  const float y = __fmul_rn(__int2float_rn(ov1 - 1), t);
+  return __float2int_rz(rintf(__fadd_rn(x, y)));
+}
+
+// ---------------------------------------------------------------------------
+// 16-byte vector <-> float conversions for the three supported element types.
+// ---------------------------------------------------------------------------
+template <typename T> struct Vec;
+
+template <> struct Vec<float> {
+  static constexpr int kElems = 4;
+  __device__ __forceinline__ static void to_float(const uint4& u, float* f) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  }
+  __device__ __forceinline__ static uint4 from_float(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]),
+                      __float_as_uint(f[2]), __float_as_uint(f[3]));
+  }
+};
+
+__device__ __forceinline__ void bf16x2_to_float(uint32_t u, float& lo, float& hi) {
+  lo = __uint_as_float(u << 16);
+  hi = __uint_as_float(u & 0xffff0000u);
+}
+
+template <> struct Vec<__nv_bfloat16> {
+  static constexpr int kElems = 8;
+  __device__ __forceinline__ static void to_float(const uint4& u, float* f) {
+    bf16x2_to_float(u.x, f[0], f[1]); bf16x2_to_float(u.y, f[2], f[3]);
+    bf16x2_to_float(u.z, f[4], f[5]); bf16x2_to_float(u.w, f[6], f[7]);
+  }
+  __device__ __forceinline__ static uint32_t pack(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static uint4 from_float(const float* f) {
+    return make_uint4(pack(f[0], f[1]), pack(f[2], f[3]), pack(f[4], f[5]), pack(f[6], f[7]));
+  }
+};
+
+template <> struct Vec<__half> {
+  static constexpr int kElems = 8;
+  __device__ __forceinline__ static void cvt2(uint32_t u, float& lo, float& hi) {
+    __half2 h = *reinterpret_cast<__half2*>(&u);
+    float2 f = __half22float2(h);
+    lo = f.x; hi = f.y;
+  }
+  __device__ __forceinline__ static void to_float(const uint4& u, float* f) {
+    cvt2(u.x, f[0], f[1]); cvt2(u.y, f[2], f[3]); cvt2(u.z, f[4], f[5]); cvt2(u.w, f[6], f[7]);
+  }
+  __device__ __forceinline__ static uint32_t pack(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static uint4 from_float(const float* f) {
+    return make_uint4(pack(f[0], f[1]), pack(f[2], f[3]), pack(f[4], f[5]), pack(f[6], f[7]));
+  }
+};
+
+__device__ __forceinline__ uint4 ldg16(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// Read-only load that is not kept in L1 (streamed operands such as Q rows of
+// the query being processed, or the output/gradient rows).
+__device__ __forceinline__ uint4 ldg16_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void stg16(void* p, const uint4& v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+// Butterfly "transpose-reduce": every lane of an aligned group of LPR lanes
+// holds LPR partial sums v[0..LPR); afterwards lane r of the group holds in
+// v[0] the total of index r over the group.  Costs LPR-1 shuffles per lane.
+template <int LPR>
+__device__ __forceinline__ void transpose_reduce(float* v, int lane) {
+#pragma unroll
+  for (int o = LPR / 2, n = LPR; o >= 1; o >>= 1, n >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = upper ? v[i] : v[i + n / 2];
+      const float keep = upper ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+}
+
+template <int LPR>
+__device__ __forceinline__ float group_allreduce_sum(float x) {
+#pragma unroll
+  for (int o = LPR / 2; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+}  // namespace esa

@@ -1,0 +1,443 @@
+// Gather kernels (CUDA cores) for elastic sparse attention on sm_100a.
+//
+// Every (query row, head) pair attends to exactly w keys whose positions are
+// computed on the fly from the pattern (no index buffers in HBM).  One warp
+// owns one pair at a time.  A key/value row of D elements is read as 16-byte
+// vectors by a group of LPR lanes (RPW = 32 / LPR rows per warp load), so
+// every load instruction touches whole 128-byte lines.  Dot products are
+// finished with a butterfly transpose-reduce that leaves one slot's score per
+// lane after LPR - 1 shuffles for a sub-chunk of 32 slots.
+//
+// Forward   (reference kernel :117-166):  O = softmax(s) V,  s = q.k * scale,
+//           plus the base-2 log-sum-exp per row (replaces the reference's
+//           separate L = sum exp and M = max outputs, :165-166).
+// Backward, query side (reference :169-233 without the atomics): recompute
+//           s, p = exp(s - lse), dp = dO.v, dS = p (dp - dO.o); write
+//           (p, dS*scale) per (row, slot) to a workspace and dQ = scale dS K.
+// Backward, key side: dK_j = sum dS*scale q_i, dV_j = sum p dO_i over the
+//           (row i, slot k) users of key j, enumerated through the transposed
+//           index: for a fixed head and slot, the key index is non-decreasing
+//           in the query position, so the users of key j in one slot column
+//           are one contiguous run of query rows, found by binary / galloping
+//           search.  No atomics: each key row is owned by one warp.
+#pragma once
+#include "esa_params.h"
+
+namespace esa {
+
+template <typename T, int D>
+struct Layout {
+  static constexpr int EPL = Vec<T>::kElems;  // elements per 16-byte vector
+  static constexpr int LPR = D / EPL;         // lanes per row
+  static constexpr int RPW = 32 / LPR;        // rows per warp load
+  static_assert(D % EPL == 0, "head_dim must fill whole 16-byte vectors");
+  static_assert(LPR >= 1 && LPR <= 32 && (32 % LPR) == 0, "unsupported head_dim");
+};
+
+__device__ __forceinline__ int query_pos(const AttnParams& p, int j) {
+  return p.rows ? (int)p.rows[j] : p.row_offset + j;
+}
+
+// Fills sidx[0..wpad) with the k/v buffer row of each slot of a pair, -1 for
+// masked slots (reference :126-131: causal mask and bounds) and padding.
+__device__ __forceinline__ void fill_slot_rows(const AttnParams& p, int pos, int h, int wpad,
+                                               int lane, int* sidx) {
+  const RowWin rw = row_window(p.pat, pos);
+  const float t = head_weight(p.pat, h);
+  const float omt = __fsub_rn(1.f, t);
+  for (int k = lane; k < wpad; k += 32) {
+    int row = -1;
+    if (k < p.pat.w) {
+      const int raw = raw_index(rw, k, t, omt);
+      if (raw <= pos) {                              // causal mask (:532)
+        const int c = min(raw, p.kv_len - 1);        // clamp (:615)
+        row = c - p.kv_offset;
+        if (row < 0 || row >= p.kv_rows) {
+          if (p.err) atomicOr(p.err, kErrKvRange);
+          row = -1;
+        }
+      }
+    }
+    sidx[k] = row;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Forward.
+// grid = (ceil(n_rows / rows_per_cta), Hkv, B); block = NW warps; the pairs of
+// a CTA are its rows x the G query heads of one KV head, head-minor, so the
+// warps running together read neighbouring rows of the same K/V head.
+// ---------------------------------------------------------------------------
+template <typename T, int D, int NW>
+__global__ void __launch_bounds__(NW * 32)
+fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
+  using L = Layout<T, D>;
+  using V = Vec<T>;
+  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int w = p.pat.w;
+  const int wpad = (w + 31) & ~31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* sidx = reinterpret_cast<int*>(smem_raw) + warp * 2 * wpad;
+  float* ssc = reinterpret_cast<float*>(sidx + wpad);
+  const int g = lane / LPR, r = lane % LPR;
+  const int hkv = blockIdx.y, b = blockIdx.z;
+  const int row0 = blockIdx.x * rows_per_cta;
+  const int n_pairs = rows_per_cta * p.G;
+  const T* Kb = reinterpret_cast<const T*>(p.k) + b * p.skb + hkv * p.skh + r * EPL;
+  const T* Vb = reinterpret_cast<const T*>(p.v) + b * p.svb + hkv * p.svh + r * EPL;
+
+  for (int pr = warp; pr < n_pairs; pr += NW) {
+    const int j = row0 + pr / p.G;
+    if (j >= p.n_rows) break;
+    const int h = hkv * p.G + pr % p.G;
+    const int pos = query_pos(p, j);
+    fill_slot_rows(p, pos, h, wpad, lane, sidx);
+
+    float qf[EPL];
+    {
+      const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh +
+                      (int64_t)j * p.sqs + r * EPL;
+      V::to_float(ldg16_stream(qrow), qf);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) qf[e] *= p.scale_log2;
+    }
+    __syncwarp();
+
+    // Scores (base-2 scaled), one slot per lane per sub-chunk of 32 slots.
+    float mloc = -INFINITY;
+    for (int s0 = 0; s0 < wpad; s0 += 32) {
+      float part[LPR];
+#pragma unroll
+      for (int m = 0; m < LPR; ++m) {
+        const int row = sidx[s0 + m * RPW + g];
+        float acc = 0.f;
+        if (row >= 0) {
+          float kf[EPL];
+          V::to_float(ldg16(Kb + (int64_t)row * p.sks), kf);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) acc = fmaf(qf[e], kf[e], acc);
+        }
+        part[m] = acc;
+      }
+      transpose_reduce<LPR>(part, lane);
+      const int k = s0 + r * RPW + g;
+      const float s = sidx[k] >= 0 ? part[0] : -INFINITY;
+      ssc[k] = s;
+      mloc = fmaxf(mloc, s);
+    }
+    float mx = warp_max(mloc);
+    mx = mx == -INFINITY ? 0.f : mx;
+    __syncwarp();
+    float lsum = 0.f;
+    for (int k = lane; k < wpad; k += 32) {
+      const float e = exp2f(ssc[k] - mx);
+      ssc[k] = e;
+      lsum += e;
+    }
+    const float l = warp_sum(lsum);
+    __syncwarp();
+
+    float acc[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+    for (int s0 = 0; s0 < wpad; s0 += 32) {
+#pragma unroll
+      for (int m = 0; m < LPR; ++m) {
+        const int k = s0 + m * RPW + g;
+        const int row = sidx[k];
+        if (row >= 0) {
+          const float pk = ssc[k];
+          float vf[EPL];
+          V::to_float(ldg16(Vb + (int64_t)row * p.svs), vf);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pk, vf[e], acc[e]);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = LPR; o < 32; o <<= 1)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+    if (g == 0) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[e] *= inv;
+      T* orow = reinterpret_cast<T*>(p.o) + b * p.sob + h * p.soh + (int64_t)j * p.sos + r * EPL;
+      stg16(orow, V::from_float(acc));
+    }
+    if (lane == 0) p.lse[((int64_t)b * p.Hq + h) * p.n_rows + j] = mx + log2f(l);
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward, query side: dQ and the (p, dS*scale) workspace.
+// Same grid and pair order as the forward.
+// ---------------------------------------------------------------------------
+template <typename T, int D, int NW>
+__global__ void __launch_bounds__(NW * 32)
+bwd_query_kernel(const AttnParams p, int rows_per_cta) {
+  using L = Layout<T, D>;
+  using V = Vec<T>;
+  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int w = p.pat.w;
+  const int wpad = (w + 31) & ~31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* sidx = reinterpret_cast<int*>(smem_raw) + warp * 2 * wpad;
+  float* sds = reinterpret_cast<float*>(sidx + wpad);
+  const int g = lane / LPR, r = lane % LPR;
+  const int hkv = blockIdx.y, b = blockIdx.z;
+  const int row0 = blockIdx.x * rows_per_cta;
+  const int n_pairs = rows_per_cta * p.G;
+  const int n = p.n_rows;
+  const T* Kb = reinterpret_cast<const T*>(p.k) + b * p.skb + hkv * p.skh + r * EPL;
+  const T* Vb = reinterpret_cast<const T*>(p.v) + b * p.svb + hkv * p.svh + r * EPL;
+
+  for (int pr = warp; pr < n_pairs; pr += NW) {
+    const int j = row0 + pr / p.G;
+    if (j >= n) break;
+    const int h = hkv * p.G + pr % p.G;
+    const int pos = query_pos(p, j);
+    fill_slot_rows(p, pos, h, wpad, lane, sidx);
+
+    float qf[EPL], df[EPL];
+    float delta;
+    {
+      const int64_t jr = (int64_t)j;
+      const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh + jr * p.sqs + r * EPL;
+      const T* drow = reinterpret_cast<const T*>(p.dout) + b * p.sdob + h * p.sdoh + jr * p.sdos + r * EPL;
+      const T* orow = reinterpret_cast<const T*>(p.o) + b * p.sob + h * p.soh + jr * p.sos + r * EPL;
+      float of[EPL];
+      V::to_float(ldg16_stream(qrow), qf);
+      V::to_float(ldg16_stream(drow), df);
+      V::to_float(ldg16_stream(orow), of);
+      float dd = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        qf[e] *= p.scale_log2;
+        dd = fmaf(df[e], of[e], dd);
+      }
+      delta = group_allreduce_sum<LPR>(dd);   // rowsum(dO * O), every group holds it
+    }
+    const float lse2 = p.lse[((int64_t)b * p.Hq + h) * n + j];
+    float2* pds_row = p.pds + ((int64_t)(b * p.Hq + h) * w) * n + j;
+    __syncwarp();
+
+    for (int s0 = 0; s0 < wpad; s0 += 32) {
+      float ps[LPR], pp[LPR];
+#pragma unroll
+      for (int m = 0; m < LPR; ++m) {
+        const int row = sidx[s0 + m * RPW + g];
+        float a = 0.f, c = 0.f;
+        if (row >= 0) {
+          float kf[EPL], vf[EPL];
+          V::to_float(ldg16(Kb + (int64_t)row * p.sks), kf);
+          V::to_float(ldg16(Vb + (int64_t)row * p.svs), vf);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            a = fmaf(qf[e], kf[e], a);
+            c = fmaf(df[e], vf[e], c);
+          }
+        }
+        ps[m] = a;
+        pp[m] = c;
+      }
+      transpose_reduce<LPR>(ps, lane);
+      transpose_reduce<LPR>(pp, lane);
+      const int k = s0 + r * RPW + g;
+      float pk = 0.f, dsk = 0.f;
+      if (sidx[k] >= 0) {
+        pk = exp2f(ps[0] - lse2);
+        dsk = pk * (pp[0] - delta) * p.scale;
+      }
+      if (k < w) pds_row[(int64_t)k * n] = make_float2(pk, dsk);
+      sds[k] = dsk;
+    }
+    __syncwarp();
+
+    float acc[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+    for (int s0 = 0; s0 < wpad; s0 += 32) {
+#pragma unroll
+      for (int m = 0; m < LPR; ++m) {
+        const int k = s0 + m * RPW + g;
+        const int row = sidx[k];
+        if (row >= 0) {
+          const float dsk = sds[k];
+          float kf[EPL];
+          V::to_float(ldg16(Kb + (int64_t)row * p.sks), kf);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) acc[e] = fmaf(dsk, kf[e], acc[e]);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = LPR; o < 32; o <<= 1)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+    if (g == 0) {
+      T* dqrow = reinterpret_cast<T*>(p.dq) + b * p.sdqb + h * p.sdqh + (int64_t)j * p.sdqs + r * EPL;
+      stg16(dqrow, V::from_float(acc));
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward, key side, for query head (hkv * G + head_in_group) of every group.
+// grid = (ceil(kv_rows / (NW * RW)), Hkv, B); warp owns RW consecutive key
+// rows; lanes own slot columns k = lane + 32 * cc.  With G > 1 the G launches
+// run in order on one stream and accumulate into the fp32 workspace; the last
+// one writes dK / dV in the input dtype.
+// ---------------------------------------------------------------------------
+template <typename T, int D, int NW, int RW>
+__global__ void __launch_bounds__(NW * 32)
+bwd_key_kernel(const AttnParams p) {
+  using L = Layout<T, D>;
+  using V = Vec<T>;
+  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int w = p.pat.w;
+  const int ncol = (w + 31) >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* scur = reinterpret_cast<int*>(smem_raw) + warp * ncol * 32;
+  const int g = lane / LPR, r = lane % LPR;
+  const int hkv = blockIdx.y, b = blockIdx.z;
+  const int h = hkv * p.G + p.head_in_group;
+  const int lr0 = (blockIdx.x * NW + warp) * RW;
+  if (lr0 >= p.kv_rows) return;
+  const int lr1 = min(lr0 + RW, p.kv_rows);
+  const int n = p.n_rows;
+  const float t = head_weight(p.pat, h);
+  const float omt = __fsub_rn(1.f, t);
+  const int64_t* srows = p.sorted_rows ? p.sorted_rows : p.rows;
+  const int kvmax = p.kv_len - 1;
+  auto cidx = [&](int jq, int k) -> int {
+    const int pos = srows ? (int)srows[jq] : p.row_offset + jq;
+    return min(raw_index(row_window(p.pat, pos), k, t, omt), kvmax);
+  };
+
+  // Cursor of each owned column: first query slot whose key is >= row lr0.
+  {
+    const int P0 = p.kv_offset + lr0;
+    for (int cc = 0; cc < ncol; ++cc) {
+      const int k = lane + 32 * cc;
+      int lo = n;
+      if (k < w) {
+        int a = 0, e = n;
+        while (a < e) {
+          const int mid = (a + e) >> 1;
+          if (cidx(mid, k) < P0) a = mid + 1; else e = mid;
+        }
+        lo = a;
+      }
+      scur[cc * 32 + lane] = lo;
+    }
+  }
+
+  const T* qbase = reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh + r * EPL;
+  const T* dbase = reinterpret_cast<const T*>(p.dout) + b * p.sdob + h * p.sdoh + r * EPL;
+  const float2* pdsb = p.pds + (int64_t)(b * p.Hq + h) * w * n;
+
+  for (int lr = lr0; lr < lr1; ++lr) {
+    const int P = p.kv_offset + lr;
+    float adk[EPL], adv[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) { adk[e] = 0.f; adv[e] = 0.f; }
+
+    for (int cc = 0; cc < ncol; ++cc) {
+      const int k = lane + 32 * cc;
+      const int start = scur[cc * 32 + lane];
+      int len = 0;
+      if (k < w && start < n && cidx(start, k) == P) {
+        // Gallop to the end of the run of query slots that use key P.
+        int lo = start, step = 1;
+        while (lo + step < n && cidx(lo + step, k) == P) { lo += step; step <<= 1; }
+        int hi = min(lo + step, n);
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (cidx(mid, k) == P) lo = mid; else hi = mid;
+        }
+        len = hi - start;
+        scur[cc * 32 + lane] = hi;
+      }
+      // Flatten the lanes' runs: exclusive prefix of run lengths.
+      int off = len;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, off, o);
+        if (lane >= o) off += y;
+      }
+      const int total = __shfl_sync(0xffffffffu, off, 31);
+      off -= len;
+      for (int u0 = 0; u0 < total; u0 += RPW) {
+        int owner = 0;
+#pragma unroll
+        for (int gg = 0; gg < RPW; ++gg) {
+          const unsigned bm = __ballot_sync(0xffffffffu, len > 0 && off <= u0 + gg);
+          if (gg == g) owner = bm ? 31 - __clz(bm) : 0;
+        }
+        const int o_start = __shfl_sync(0xffffffffu, start, owner);
+        const int o_off = __shfl_sync(0xffffffffu, off, owner);
+        const int u = u0 + g;
+        if (u < total) {
+          const int jq = o_start + (u - o_off);
+          const int qi = p.row_perm ? (int)p.row_perm[jq] : jq;
+          const int kk = owner + 32 * cc;
+          const float2 pd = pdsb[(int64_t)kk * n + qi];
+          float qf[EPL], df[EPL];
+          V::to_float(ldg16(qbase + (int64_t)qi * p.sqs), qf);
+          V::to_float(ldg16(dbase + (int64_t)qi * p.sdos), df);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            adk[e] = fmaf(pd.y, qf[e], adk[e]);
+            adv[e] = fmaf(pd.x, df[e], adv[e]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = LPR; o < 32; o <<= 1)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        adk[e] += __shfl_xor_sync(0xffffffffu, adk[e], o);
+        adv[e] += __shfl_xor_sync(0xffffffffu, adv[e], o);
+      }
+    if (g == 0) {
+      T* dkrow = reinterpret_cast<T*>(p.dk) + b * p.sdkb + hkv * p.sdkh + (int64_t)lr * p.sdks + r * EPL;
+      T* dvrow = reinterpret_cast<T*>(p.dv) + b * p.sdvb + hkv * p.sdvh + (int64_t)lr * p.sdvs + r * EPL;
+      if (p.G == 1) {
+        stg16(dkrow, V::from_float(adk));
+        stg16(dvrow, V::from_float(adv));
+      } else {
+        const int64_t plane = (int64_t)p.B * p.Hkv * p.kv_rows * D;
+        float* ak = p.acc + (((int64_t)b * p.Hkv + hkv) * p.kv_rows + lr) * D + r * EPL;
+        float* av = ak + plane;
+        if (p.head_in_group > 0) {
+#pragma unroll
+          for (int e = 0; e < EPL; e += 4) {
+            const float4 x = *reinterpret_cast<const float4*>(ak + e);
+            const float4 y = *reinterpret_cast<const float4*>(av + e);
+            adk[e] += x.x; adk[e + 1] += x.y; adk[e + 2] += x.z; adk[e + 3] += x.w;
+            adv[e] += y.x; adv[e + 1] += y.y; adv[e + 2] += y.z; adv[e + 3] += y.w;
+          }
+        }
+        if (p.head_in_group == p.G - 1) {
+          stg16(dkrow, V::from_float(adk));
+          stg16(dvrow, V::from_float(adv));
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPL; e += 4) {
+            *reinterpret_cast<float4*>(ak + e) = make_float4(adk[e], adk[e + 1], adk[e + 2], adk[e + 3]);
+            *reinterpret_cast<float4*>(av + e) = make_float4(adv[e], adv[e + 1], adv[e + 2], adv[e + 3]);
+          }
+        }
+      }
+    }
+  }
+}
+
+}  // namespace esa

@@ -1,0 +1,46 @@
+// Launch parameters shared by the host entry points and the kernels.
+#pragma once
+#include <stdint.h>
+
+#include "esa_common.cuh"
+
+namespace esa {
+
+struct AttnParams {
+  // Shapes.
+  int B, Hq, Hkv, G, D;
+  int n_rows;     // query rows handed to the launch (Lq, or len(cache_position))
+  int kv_len;     // kv_seq_len of the call: indices are clamped to kv_len - 1 (reference :615)
+  int kv_offset;  // absolute position held by row 0 of the k/v (and dk/dv) buffers
+  int kv_rows;    // rows present in the k/v buffers
+  int row_offset; // position of query row j is row_offset + j when rows == nullptr
+  const int64_t* rows;  // optional explicit positions [n_rows] (decode: cache_position)
+  Pattern pat;
+  float scale;       // softmax scale (reference self.scaling = head_dim ** -0.5, :444)
+  float scale_log2;  // scale * log2(e)
+
+  // Forward operands; strides are in elements, the head_dim axis is contiguous.
+  const void* q; int64_t sqb, sqh, sqs;
+  const void* k; int64_t skb, skh, sks;
+  const void* v; int64_t svb, svh, svs;
+  void* o;       int64_t sob, soh, sos;
+  float* lse;    // [B, Hq, n_rows] base-2 log-sum-exp of the scaled scores
+
+  // Backward operands.
+  const void* dout; int64_t sdob, sdoh, sdos;
+  void* dq;         int64_t sdqb, sdqh, sdqs;
+  void* dk;         int64_t sdkb, sdkh, sdks;
+  void* dv;         int64_t sdvb, sdvh, sdvs;
+  float2* pds;      // workspace [B, Hq, w, n_rows]: (p, dS * scale) per (row, slot)
+  float* acc;       // workspace fp32 [2, B, Hkv, kv_rows, D] (only when G > 1)
+  const int64_t* sorted_rows;  // optional positions sorted ascending (key side)
+  const int64_t* row_perm;     // optional: sorted slot -> query row of the tensors
+  int head_in_group;           // key-side launch: which query head of each group
+  int* err;                    // optional device error word (bit flags)
+};
+
+enum ErrBits : int {
+  kErrKvRange = 1,  // an index fell outside the k/v rows handed to the launch
+};
+
+}  // namespace esa

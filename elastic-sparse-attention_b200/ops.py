@@ -1,0 +1,134 @@
+"""Tensor-level calls into libesa_b200 (forward, backward, pattern, audit).
+
+Each function allocates its outputs and workspace with torch (the C ABI never
+allocates), then launches on the current CUDA stream of the input's device.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+# Positions are handled in exact float32 arithmetic only below 2^24.
+MAX_POSITION = 1 << 24
+
+
+@dataclass(frozen=True)
+class PatternSpec:
+    """The elastic pattern of one layer (reference __init__ arguments, :375-386)."""
+    layer_idx: int
+    num_hidden_layers: int
+    attention_length: int
+
+
+def _aligned(t: torch.Tensor) -> bool:
+    es = t.element_size()
+    return (t.stride(-1) == 1 and t.data_ptr() % 16 == 0
+            and all((s * es) % 16 == 0 for s in t.stride()[:3]))
+
+
+def as_kernel_operand(t: torch.Tensor) -> torch.Tensor:
+    """Return ``t`` if the kernels can read it in place, else a contiguous copy
+    (the reference always calls ``.contiguous()``, :244-245)."""
+    return t if _aligned(t) else t.contiguous()
+
+
+def _check_device(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    if dev.type != "cuda":
+        raise RuntimeError("elastic sparse attention (B200) runs on CUDA tensors only; "
+                           "there is no CPU fallback")
+    for t in ts[1:]:
+        if t.device != dev:
+            raise RuntimeError("all operands must be on the same CUDA device")
+    return dev
+
+
+def pattern_indices(num_heads: int, spec: PatternSpec, n_rows: int, device: torch.device,
+                    rows: torch.Tensor | None = None, row_offset: int = 0,
+                    clamp_len: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """(idx, mask) int64 [H, n_rows, w] built on ``device`` by the pattern kernel."""
+    lib = _lib.load()
+    w = spec.attention_length
+    idx = torch.empty((num_heads, n_rows, w), dtype=torch.int64, device=device)
+    mask = torch.empty_like(idx)
+    if rows is not None:
+        rows = rows.to(device=device, dtype=torch.int64).contiguous()
+    with torch.cuda.device(device):
+        _lib.check(lib.esa_pattern(num_heads, w, spec.layer_idx, spec.num_hidden_layers, n_rows,
+                                   _lib.ptr(rows), row_offset, clamp_len, idx.data_ptr(),
+                                   mask.data_ptr(), _lib.stream_handle(device)), "esa_pattern")
+    return idx, mask
+
+
+def pattern_audit(num_heads: int, spec: PatternSpec, seq_len: int, device: torch.device) -> int:
+    """Number of decreasing steps in the per-slot index columns (0 expected)."""
+    lib = _lib.load()
+    count = torch.zeros(1, dtype=torch.int64, device=device)
+    with torch.cuda.device(device):
+        _lib.check(lib.esa_pattern_audit(num_heads, spec.attention_length, spec.layer_idx,
+                                         spec.num_hidden_layers, seq_len, count.data_ptr(),
+                                         _lib.stream_handle(device)), "esa_pattern_audit")
+    return int(count.item())
+
+
+def _problem(q, k, spec: PatternSpec, scale: float, rows, row_offset: int, kv_len: int,
+             kv_offset: int):
+    B, Hq, Lq, D = q.shape
+    return _lib.problem(dtype=q.dtype, batch=B, num_heads=Hq, num_kv_heads=k.shape[1], head_dim=D,
+                        attn_length=spec.attention_length, layer_idx=spec.layer_idx,
+                        num_hidden_layers=spec.num_hidden_layers, q_len=Lq, kv_len=kv_len,
+                        kv_offset=kv_offset, kv_rows=k.shape[2], row_offset=row_offset,
+                        rows=rows, scale=scale)
+
+
+def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: PatternSpec, scale: float,
+            rows: torch.Tensor | None = None, row_offset: int = 0, kv_len: int | None = None,
+            kv_offset: int = 0, out: torch.Tensor | None = None):
+    """Forward pass.  Returns (o [B, Hq, Lq, D] as a view of a [B, Lq, Hq, D]
+    buffer, lse float32 [B, Hq, Lq] base 2)."""
+    dev = _check_device(q, k, v)
+    B, Hq, Lq, D = q.shape
+    if out is None:
+        out = torch.empty((B, Lq, Hq, D), dtype=q.dtype, device=dev).transpose(1, 2)
+    lse = torch.empty((B, Hq, Lq), dtype=torch.float32, device=dev)
+    pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
+                  kv_offset)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.esa_forward(ctypes.byref(pb), _lib.tensor4(q), _lib.tensor4(k),
+                                   _lib.tensor4(v), _lib.tensor4(out), lse.data_ptr(),
+                                   _lib.stream_handle(dev)), "esa_forward")
+    return out, lse
+
+
+def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
+             rows: torch.Tensor | None = None, row_offset: int = 0, kv_len: int | None = None,
+             kv_offset: int = 0, sorted_rows=None, row_perm=None, workspace=None):
+    """Backward pass.  Returns (dq, dk, dv) in the input dtype."""
+    dev = _check_device(q, k, v, o, lse, dout)
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
+                  kv_offset)
+    lib = _lib.load()
+    need = lib.esa_backward_workspace_size(ctypes.byref(pb))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(lib.esa_backward(ctypes.byref(pb), _lib.tensor4(q), _lib.tensor4(k),
+                                    _lib.tensor4(v), _lib.tensor4(o), lse.data_ptr(),
+                                    _lib.tensor4(dout), _lib.tensor4(dq), _lib.tensor4(dk),
+                                    _lib.tensor4(dv), _lib.ptr(sorted_rows), _lib.ptr(row_perm),
+                                    workspace.data_ptr(), workspace.numel(),
+                                    _lib.stream_handle(dev)), "esa_backward")
+    return dq, dk, dv
+
+
+def backward_workspace_bytes(q, k, spec: PatternSpec, kv_len: int | None = None) -> int:
+    pb = _problem(q, k, spec, 1.0, None, 0, k.shape[2] if kv_len is None else kv_len, 0)
+    return int(_lib.load().esa_backward_workspace_size(ctypes.byref(pb)))

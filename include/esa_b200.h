@@ -1,0 +1,150 @@
+/*
+ * esa_b200.h -- C ABI of the B200-native elastic sparse attention library
+ * (libesa_b200.so).  Plain pointers and sizes only; every buffer is device
+ * memory owned by the caller; no entry point allocates device memory.  All
+ * launches go to the stream passed in (a cudaStream_t, NULL = legacy default
+ * stream) and are asynchronous.  Functions return ESA_OK (0) or a negative
+ * code; esa_last_error() gives the message of the last failure on the
+ * calling thread.
+ *
+ * Tensor convention: an attention operand of logical shape [B, H, L, D] is
+ * described by esa_tensor_t {data, stride_b, stride_h, stride_s} with strides
+ * in elements and the D axis contiguous.  Base pointers and the three strides
+ * (times the element size) must be multiples of 16 bytes.
+ *
+ * Reference interfaces replaced (HighCWu/elastic-sparse-attention,
+ * elastic_sparse_attention.py):
+ *   esa_pattern          _create_elastic_sparse_indices          :470-535
+ *                        + _get_prepared_indices_and_mask slicing :574-590, :600-615
+ *   esa_forward          ElasticSparseAttentionFunction.forward  :241-297
+ *                        (Triton kernel, IS_BWD=False            :117-166)
+ *   esa_backward         ElasticSparseAttentionFunction.backward :300-339
+ *                        (Triton kernel, IS_BWD=True             :169-233)
+ */
+#ifndef ESA_B200_H
+#define ESA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ESA_OK 0
+#define ESA_ERR_INVALID (-1)     /* bad argument, shape, stride or alignment */
+#define ESA_ERR_UNSUPPORTED (-2) /* dtype / head_dim combination not built */
+#define ESA_ERR_CUDA (-3)        /* a CUDA runtime call failed */
+#define ESA_ERR_WORKSPACE (-4)   /* workspace smaller than esa_backward_workspace_size */
+
+typedef enum {
+  ESA_DTYPE_F32 = 0,
+  ESA_DTYPE_BF16 = 1,
+  ESA_DTYPE_F16 = 2
+} esa_dtype_t;
+
+typedef struct {
+  void* data;
+  int64_t stride_b;
+  int64_t stride_h;
+  int64_t stride_s;
+} esa_tensor_t;
+
+/*
+ * One attention call.  Mirrors the reference module's arguments:
+ *   num_heads / num_kv_heads / head_dim / attention_length / layer_idx /
+ *   num_hidden_layers  -- ElasticSparseAttention.__init__ (:375-386)
+ *   q_len, kv_len      -- query_states.shape[2], key_states.shape[2]
+ *   rows               -- cache_position (:602-608) as device int64 [q_len],
+ *                         or NULL: query row j is position row_offset + j
+ *                         (the reference slices rows [:q_len], i.e. offset 0)
+ *   kv_offset, kv_rows -- the k/v (and dk/dv) buffers hold positions
+ *                         [kv_offset, kv_offset + kv_rows); for a plain call
+ *                         kv_offset = 0 and kv_rows = kv_len
+ *   scale              -- softmax scale, the reference uses head_dim ** -0.5
+ */
+typedef struct {
+  int32_t dtype;
+  int32_t batch;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t attn_length;
+  int32_t layer_idx;
+  int32_t num_hidden_layers;
+  int64_t q_len;
+  int64_t kv_len;
+  int64_t kv_offset;
+  int64_t kv_rows;
+  int64_t row_offset;
+  const int64_t* rows;
+  float scale;
+  int32_t reserved;
+} esa_problem_t;
+
+/* Library version, e.g. 100 for 0.1.0. */
+int esa_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* esa_last_error(void);
+
+/*
+ * Pattern buffers, bit-exact with the reference: idx/mask int64 [H, n_rows, w]
+ * for the query positions rows[r] (device int64, or row_offset + r when rows
+ * is NULL).  clamp_len > 0 clamps indices to [0, clamp_len - 1] as
+ * _triton_forward does (:615); clamp_len <= 0 gives the raw module buffers
+ * sparse_attention_indices / sparse_causal_mask (:465-468, :532-535).
+ * Replaces _create_elastic_sparse_indices (:470-535).
+ */
+int esa_pattern(int32_t num_heads, int32_t attn_length, int32_t layer_idx,
+                int32_t num_hidden_layers, int64_t n_rows, const int64_t* rows,
+                int64_t row_offset, int64_t clamp_len, int64_t* idx, int64_t* mask,
+                void* stream);
+
+/*
+ * Counts (head, row, slot) where the raw slot index decreases from query
+ * position r - 1 to r, r < seq_len, and adds the count to *d_count (device
+ * uint64, caller zeroes it).  Zero is the precondition of esa_backward's
+ * key-side enumeration; the library's Python module checks it once per
+ * pattern.  No reference counterpart (the reference backward uses atomics).
+ */
+int esa_pattern_audit(int32_t num_heads, int32_t attn_length, int32_t layer_idx,
+                      int32_t num_hidden_layers, int64_t seq_len,
+                      unsigned long long* d_count, void* stream);
+
+/*
+ * Forward.  q [B, Hq, q_len, D], k/v [B, Hkv, kv_rows, D], o [B, Hq, q_len, D]
+ * (any strides per the tensor convention; the Python module passes an o laid
+ * out as [B, q_len, Hq, D] so that its final reshape is free), lse float32
+ * [B, Hq, q_len] contiguous: base-2 log-sum-exp of the scaled scores
+ * (replaces the reference's separate L and M outputs, :255-257, :165-166).
+ * Replaces ElasticSparseAttentionFunction.forward (:241-297).
+ */
+int esa_forward(const esa_problem_t* prob, esa_tensor_t q, esa_tensor_t k, esa_tensor_t v,
+                esa_tensor_t o, float* lse, void* stream);
+
+/* Bytes of workspace esa_backward needs for this problem. */
+size_t esa_backward_workspace_size(const esa_problem_t* prob);
+
+/*
+ * Backward.  Takes the forward's o and lse and the upstream gradient dout
+ * (all [B, Hq, q_len, D]); writes dq [B, Hq, q_len, D] and dk/dv
+ * [B, Hkv, kv_rows, D], fully (no zero-initialisation needed, no atomics).
+ * When rows != NULL the key side needs the positions sorted ascending:
+ * pass sorted_rows (device int64 [q_len], ascending) and row_perm (device
+ * int64 [q_len], sorted slot -> query row), or NULL for both when rows is
+ * already sorted.  workspace: device memory of esa_backward_workspace_size()
+ * bytes, 256-byte aligned.
+ * Replaces ElasticSparseAttentionFunction.backward (:300-339).
+ */
+int esa_backward(const esa_problem_t* prob, esa_tensor_t q, esa_tensor_t k, esa_tensor_t v,
+                 esa_tensor_t o, const float* lse, esa_tensor_t dout, esa_tensor_t dq,
+                 esa_tensor_t dk, esa_tensor_t dv, const int64_t* sorted_rows,
+                 const int64_t* row_perm, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ESA_B200_H */

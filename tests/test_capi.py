@@ -1,0 +1,120 @@
+"""CPU: the C-ABI library loads, exports every symbol the header declares, its
+struct layout matches the ctypes mirror, and argument validation reports
+errors without touching a GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "esa_b200.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(esa_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_library_exports_header_symbols(esa):
+    lib = esa._lib.load()
+    names = header_functions()
+    assert set(names) == set(esa._lib.EXPORTED), names
+    for name in names:
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", esa._lib.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (esa_\w+)", out))
+    assert set(names) <= exported
+
+
+def test_struct_layout_matches_header(tmp_path, esa):
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "esa_b200.h"\n'
+        "int main(void){\n"
+        ' printf("%zu %zu %zu %zu %zu %zu %zu\\n", sizeof(esa_problem_t),'
+        " offsetof(esa_problem_t, q_len), offsetof(esa_problem_t, rows),"
+        " offsetof(esa_problem_t, scale), sizeof(esa_tensor_t),"
+        " offsetof(esa_tensor_t, stride_s), offsetof(esa_problem_t, row_offset));\n"
+        " return 0; }\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)],
+                   check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    P, T = esa._lib.EsaProblem, esa._lib.EsaTensor
+    want = [ctypes.sizeof(P), P.q_len.offset, P.rows.offset, P.scale.offset, ctypes.sizeof(T),
+            T.stride_s.offset, P.row_offset.offset]
+    assert got == want
+
+
+def _problem(esa, **kw):
+    base = dict(dtype=esa._lib.DTYPES[__import__("torch").bfloat16], batch=1, num_heads=4,
+                num_kv_heads=2, head_dim=128, attn_length=64, layer_idx=3, num_hidden_layers=8,
+                q_len=16, kv_len=16, kv_offset=0, kv_rows=16, row_offset=0, rows=None,
+                scale=128 ** -0.5, reserved=0)
+    base.update(kw)
+    return esa._lib.EsaProblem(**base)
+
+
+@pytest.mark.parametrize("kw,code,frag", [
+    (dict(num_kv_heads=3), -1, "divisible"),
+    (dict(head_dim=48), -2, "head_dim"),
+    (dict(attn_length=0), -2, "attention_length"),
+    (dict(attn_length=4096), -2, "attention_length"),
+    (dict(kv_len=1 << 25), -2, "2^24"),
+    (dict(dtype=7), -1, "dtype"),
+    (dict(scale=float("inf")), -1, "scale"),
+])
+def test_forward_rejects_bad_problems(esa, kw, code, frag):
+    lib = esa._lib.load()
+    pb = _problem(esa, **kw)
+    t = esa._lib.EsaTensor(16, 0, 0, 0)
+    rc = lib.esa_forward(ctypes.byref(pb), t, t, t, t, 16, None)
+    assert rc == code
+    assert frag in lib.esa_last_error().decode()
+
+
+def test_forward_rejects_misaligned_tensor(esa):
+    lib = esa._lib.load()
+    pb = _problem(esa)
+    good = esa._lib.EsaTensor(1 << 20, 4096, 1024, 128)
+    bad = esa._lib.EsaTensor((1 << 20) + 2, 4096, 1024, 128)
+    assert lib.esa_forward(ctypes.byref(pb), bad, good, good, good, 1 << 20, None) == -1
+    assert "16-byte" in lib.esa_last_error().decode()
+    odd = esa._lib.EsaTensor(1 << 20, 4096, 1024, 3)
+    assert lib.esa_forward(ctypes.byref(pb), good, odd, good, good, 1 << 20, None) == -1
+    assert "strides" in lib.esa_last_error().decode()
+
+
+def test_backward_workspace_and_checks(esa):
+    lib = esa._lib.load()
+    pb = _problem(esa)
+    need = lib.esa_backward_workspace_size(ctypes.byref(pb))
+    # (p, dS) per (batch, head, slot, row) + fp32 dK/dV accumulators for GQA
+    assert need == (1 * 4 * 64 * 16 * 8) + (2 * 1 * 2 * 16 * 128 * 4)
+    t = esa._lib.EsaTensor(1 << 20, 4096, 1024, 128)
+    rc = lib.esa_backward(ctypes.byref(pb), t, t, t, t, 1 << 20, t, t, t, t, None, None,
+                          1 << 20, need - 1, None)
+    assert rc == -4 and "workspace" in lib.esa_last_error().decode()
+    rc = lib.esa_backward(ctypes.byref(pb), t, t, t, t, 1 << 20, t, t, t, t, 1 << 21, None,
+                          1 << 20, need, None)
+    assert rc == -1 and "together" in lib.esa_last_error().decode()
+
+
+def test_empty_query_is_a_noop(esa):
+    lib = esa._lib.load()
+    pb = _problem(esa, q_len=0)
+    t = esa._lib.EsaTensor(16, 0, 0, 0)
+    assert lib.esa_forward(ctypes.byref(pb), t, t, t, t, 16, None) == 0
+
+
+def test_pattern_rejects_bad_rows(esa):
+    lib = esa._lib.load()
+    assert lib.esa_pattern(4, 64, 0, 8, 1 << 25, None, 0, 0, 16, 16, None) == -1
+    assert lib.esa_pattern(4, 0, 0, 8, 16, None, 0, 0, 16, 16, None) == -1
+    assert lib.esa_pattern(4, 64, 0, 8, 0, None, 0, 0, None, None, None) == 0

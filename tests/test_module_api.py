@@ -1,0 +1,49 @@
+"""CPU: the drop-in module keeps the reference's constructor contract and
+fails loudly (no CPU fallback) instead of computing on the host."""
+import pytest
+import torch
+
+
+def test_constructor_matches_reference_contract(esa):
+    m = esa.ElasticSparseAttention(layer_idx=2, num_hidden_layers=8, num_attention_heads=32,
+                                   head_dim=128, attention_length=64, max_seq_len=4096,
+                                   num_key_value_heads=8)
+    assert m.num_kv_groups == 4
+    assert m.scaling == 128 ** -0.5
+    assert m.implementation == "triton"
+    assert m.num_key_value_heads == 8
+    m2 = esa.ElasticSparseAttention(0, 1, 4, 64, 16, 128)
+    assert m2.num_key_value_heads == 4 and m2.num_kv_groups == 1
+    for impl in ("triton", "naive", "dense"):
+        assert esa.ElasticSparseAttention(0, 4, 4, 64, 16, 128, implementation=impl).implementation == impl
+    # state_dict stays empty: the pattern is not a persistent buffer (reference :466-468)
+    assert len(m.state_dict()) == 0
+
+
+def test_constructor_errors(esa):
+    with pytest.raises(ValueError, match="Invalid implementation 'flash'"):
+        esa.ElasticSparseAttention(0, 4, 4, 64, 16, 128, implementation="flash")
+    with pytest.raises(ValueError, match="must be divisible by"):
+        esa.ElasticSparseAttention(0, 4, 6, 64, 16, 128, num_key_value_heads=4)
+
+
+def test_forward_length_check_and_no_cpu_path(esa):
+    m = esa.ElasticSparseAttention(0, 4, 2, 32, 16, 64)
+    q = torch.randn(1, 2, 8, 32)
+    k = torch.randn(1, 2, 65, 32)
+    with pytest.raises(ValueError, match="exceeds the maximum length"):
+        m(q, k, k)
+    k = torch.randn(1, 2, 8, 32)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        m(q, k, k)
+
+
+def test_q_longer_than_kv_needs_cache_position(esa):
+    m = esa.ElasticSparseAttention(0, 4, 2, 32, 16, 64)
+    with pytest.raises(ValueError, match="needs cache_position"):
+        m(torch.randn(1, 2, 9, 32), torch.randn(1, 2, 8, 32), torch.randn(1, 2, 8, 32))
+
+
+def test_pattern_spec(esa):
+    s = esa.PatternSpec(3, 8, 64)
+    assert (s.layer_idx, s.num_hidden_layers, s.attention_length) == (3, 8, 64)
