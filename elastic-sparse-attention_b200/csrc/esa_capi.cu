@@ -52,8 +52,8 @@ esa::Pattern make_pattern(int num_heads, int w, int layer_idx, int num_hidden_la
 int elem_size(int dtype) { return dtype == ESA_DTYPE_F32 ? 4 : 2; }
 
 bool head_dim_supported(int dtype, int d) {
-  if (dtype == ESA_DTYPE_F32) return d == 32 || d == 64 || d == 128;
-  return d == 32 || d == 64 || d == 128 || d == 256;
+  if (dtype == ESA_DTYPE_F32) return d == 8 || d == 16 || d == 32 || d == 64 || d == 128;
+  return d == 8 || d == 16 || d == 32 || d == 64 || d == 128 || d == 256;
 }
 
 int check_tensor(const char* name, const esa_tensor_t& t, int esize) {
@@ -192,6 +192,8 @@ int dispatch_op(int dtype, int d, const esa::AttnParams& p, cudaStream_t s) {
   switch (dtype) {
     case ESA_DTYPE_F32:
       switch (d) {
+        case 8: return Op::template run<float, 8>(p, s);
+        case 16: return Op::template run<float, 16>(p, s);
         case 32: return Op::template run<float, 32>(p, s);
         case 64: return Op::template run<float, 64>(p, s);
         case 128: return Op::template run<float, 128>(p, s);
@@ -199,6 +201,8 @@ int dispatch_op(int dtype, int d, const esa::AttnParams& p, cudaStream_t s) {
       break;
     case ESA_DTYPE_BF16:
       switch (d) {
+        case 8: return Op::template run<__nv_bfloat16, 8>(p, s);
+        case 16: return Op::template run<__nv_bfloat16, 16>(p, s);
         case 32: return Op::template run<__nv_bfloat16, 32>(p, s);
         case 64: return Op::template run<__nv_bfloat16, 64>(p, s);
         case 128: return Op::template run<__nv_bfloat16, 128>(p, s);
@@ -207,6 +211,8 @@ int dispatch_op(int dtype, int d, const esa::AttnParams& p, cudaStream_t s) {
       break;
     case ESA_DTYPE_F16:
       switch (d) {
+        case 8: return Op::template run<__half, 8>(p, s);
+        case 16: return Op::template run<__half, 16>(p, s);
         case 32: return Op::template run<__half, 32>(p, s);
         case 64: return Op::template run<__half, 64>(p, s);
         case 128: return Op::template run<__half, 128>(p, s);

@@ -63,7 +63,7 @@ def _problem(esa, **kw):
 
 @pytest.mark.parametrize("kw,code,frag", [
     (dict(num_kv_heads=3), -1, "divisible"),
-    (dict(head_dim=48), -2, "head_dim"),
+    (dict(head_dim=48), -2, "head_dim"), (dict(head_dim=4), -2, "head_dim"),
     (dict(attn_length=0), -2, "attention_length"),
     (dict(attn_length=4096), -2, "attention_length"),
     (dict(kv_len=1 << 25), -2, "2^24"),

@@ -107,7 +107,7 @@ def test_c1_full(esa, c1_rows):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("D", [32, 64, 128, 256])
+@pytest.mark.parametrize("D", [8, 16, 32, 64, 128, 256])
 def test_dtypes_and_head_dims(esa, dtype, D):
     if dtype == torch.float32 and D == 256:
         pytest.skip("fp32 kernels cover head_dim <= 128")
