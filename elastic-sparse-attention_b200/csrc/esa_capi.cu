@@ -3,9 +3,12 @@
 // Host-side validation, workspace layout, kernel selection and launch.  No
 // entry point allocates device memory: outputs and workspace come from the
 // caller (the Python module takes them from torch's caching allocator).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <mutex>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -13,6 +16,7 @@
 #include "esa_b200.h"
 #include "esa_gather.cuh"
 #include "esa_pattern.cuh"
+#include "esa_window_tc.cuh"
 
 namespace {
 
@@ -111,6 +115,8 @@ esa::AttnParams base_params(const esa_problem_t* pb) {
   p.pat = make_pattern(pb->num_heads, pb->attn_length, pb->layer_idx, pb->num_hidden_layers);
   p.scale = pb->scale;
   p.scale_log2 = pb->scale * esa::kLog2e;
+  p.alpha_zero = pb->layer_idx == 0;   // alpha = layer_idx / max(nl - 1, 1) == 0
+  p.flags = pb->flags;
   return p;
 }
 
@@ -137,8 +143,87 @@ int prepare_smem(K kernel, size_t bytes) {
   return ESA_OK;
 }
 
+// ---- tensor-core sliding-window path (alpha == 0) -------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 4-D map {D, rows, heads, batch} of a 16-bit operand, box {64, box_rows, 1, 1},
+// 128-byte swizzle, zero fill outside the tensor.
+bool encode_map(CUtensorMap* m, const void* ptr, bool fp16, int64_t D, int64_t rows,
+                int64_t heads, int64_t batch, int64_t s_row, int64_t s_head, int64_t s_batch,
+                int box_rows) {
+  auto enc = tmap_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)heads,
+                              (cuuint64_t)batch};
+  const cuuint64_t strides[3] = {(cuuint64_t)s_row * 2, (cuuint64_t)s_head * 2,
+                                 (cuuint64_t)s_batch * 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(m, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+             const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Heads per UMMA tile for the window path, 0 when the call is not eligible.
+template <typename T, int D>
+int window_heads(const esa::AttnParams& p, bool alpha_zero, int flags) {
+  if (std::is_same<T, float>::value || D != esa::kWinHeadDim) return 0;
+  if (!alpha_zero || (flags & ESA_FLAG_GATHER_ONLY) || p.rows) return 0;
+  const int ht = (p.G % 4 == 0) ? 4 : (p.G == 2 ? 2 : 0);
+  if (!ht) return 0;
+  const int qt = esa::kWinRows / ht;
+  const int nk = (qt + p.pat.w - 1 + 15) / 16 * 16;
+  if (nk > esa::kWinMaxKeys) return 0;
+  const int64_t last = (int64_t)p.row_offset + p.n_rows;   // one past the last position
+  if (last > p.kv_len || last > (int64_t(1) << 21)) return 0;
+  if (p.kv_offset > std::max(0, p.row_offset - p.pat.w + 1) ||
+      (int64_t)p.kv_offset + p.kv_rows < last)
+    return 0;
+  if (p.sqb <= 0 || p.sqh <= 0 || p.sqs <= 0 || p.skb <= 0 || p.skh <= 0 || p.sks <= 0 ||
+      p.svb <= 0 || p.svh <= 0 || p.svs <= 0)
+    return 0;
+  return tmap_encoder() ? ht : 0;
+}
+
+template <typename T, int HT>
+int launch_window(const esa::AttnParams& p, cudaStream_t s) {
+  constexpr int QT = esa::kWinRows / HT;
+  const int nk = (QT + p.pat.w - 1 + 15) / 16 * 16;
+  const bool fp16 = std::is_same<T, __half>::value;
+  esa::WindowTmaps maps;
+  if (!encode_map(&maps.q, p.q, fp16, p.D, p.n_rows, p.Hq, p.B, p.sqs, p.sqh, p.sqb, QT) ||
+      !encode_map(&maps.k, p.k, fp16, p.D, p.kv_rows, p.Hkv, p.B, p.sks, p.skh, p.skb, nk) ||
+      !encode_map(&maps.v, p.v, fp16, p.D, p.kv_rows, p.Hkv, p.B, p.svs, p.svh, p.svb, nk))
+    return fail(ESA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the window path");
+  auto kern = esa::window_fwd_tc_kernel<T, HT>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           esa::kWinSmemBytes) != cudaSuccess)
+    return fail(ESA_ERR_CUDA, "cannot reserve shared memory for the window path");
+  dim3 grid((p.n_rows + QT - 1) / QT, p.Hkv * (p.G / HT), p.B);
+  kern<<<grid, esa::kWinThreads, esa::kWinSmemBytes, s>>>(maps, p, nk);
+  return check_launch("forward (tensor-core window)");
+}
+
 template <typename T, int D>
 int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
+  if constexpr (!std::is_same<T, float>::value && D == esa::kWinHeadDim) {
+    const int ht = window_heads<T, D>(p, p.alpha_zero, p.flags);
+    if (ht == 4) return launch_window<T, 4>(p, s);
+    if (ht == 2) return launch_window<T, 2>(p, s);
+  }
   const int rpc = rows_per_cta(p.G);
   const int wpad = (p.pat.w + 31) & ~31;
   const size_t smem = (size_t)kFwdWarps * 2 * wpad * sizeof(int);

@@ -37,6 +37,8 @@ struct AttnParams {
   const int64_t* row_perm;     // optional: sorted slot -> query row of the tensors
   int head_in_group;           // key-side launch: which query head of each group
   int* err;                    // optional device error word (bit flags)
+  bool alpha_zero;             // layer_idx == 0: the pattern is a causal window of w keys
+  int flags;                   // ESA_FLAG_* of the call
 };
 
 enum ErrBits : int {

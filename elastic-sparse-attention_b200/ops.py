@@ -76,27 +76,28 @@ def pattern_audit(num_heads: int, spec: PatternSpec, seq_len: int, device: torch
 
 
 def _problem(q, k, spec: PatternSpec, scale: float, rows, row_offset: int, kv_len: int,
-             kv_offset: int):
+             kv_offset: int, flags: int = 0):
     B, Hq, Lq, D = q.shape
     return _lib.problem(dtype=q.dtype, batch=B, num_heads=Hq, num_kv_heads=k.shape[1], head_dim=D,
                         attn_length=spec.attention_length, layer_idx=spec.layer_idx,
                         num_hidden_layers=spec.num_hidden_layers, q_len=Lq, kv_len=kv_len,
                         kv_offset=kv_offset, kv_rows=k.shape[2], row_offset=row_offset,
-                        rows=rows, scale=scale)
+                        rows=rows, scale=scale, flags=flags)
 
 
 def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: PatternSpec, scale: float,
             rows: torch.Tensor | None = None, row_offset: int = 0, kv_len: int | None = None,
-            kv_offset: int = 0, out: torch.Tensor | None = None):
+            kv_offset: int = 0, out: torch.Tensor | None = None, gather_only: bool = False):
     """Forward pass.  Returns (o [B, Hq, Lq, D] as a view of a [B, Lq, Hq, D]
-    buffer, lse float32 [B, Hq, Lq] base 2)."""
+    buffer, lse float32 [B, Hq, Lq] base 2).  ``gather_only`` keeps sliding-
+    window layers on the CUDA-core kernel (for cross-checking the two paths)."""
     dev = _check_device(q, k, v)
     B, Hq, Lq, D = q.shape
     if out is None:
         out = torch.empty((B, Lq, Hq, D), dtype=q.dtype, device=dev).transpose(1, 2)
     lse = torch.empty((B, Hq, Lq), dtype=torch.float32, device=dev)
     pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
-                  kv_offset)
+                  kv_offset, _lib.FLAG_GATHER_ONLY if gather_only else 0)
     lib = _lib.load()
     with torch.cuda.device(dev):
         _lib.check(lib.esa_forward(ctypes.byref(pb), _lib.tensor4(q), _lib.tensor4(k),

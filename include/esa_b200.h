@@ -79,8 +79,12 @@ typedef struct {
   int64_t row_offset;
   const int64_t* rows;
   float scale;
-  int32_t reserved;
+  int32_t flags;   /* ESA_FLAG_* bits, 0 by default */
 } esa_problem_t;
+
+/* flags: run every layer on the CUDA-core gather kernels, also where the
+ * tensor-core sliding-window kernel would apply (for cross-checking paths). */
+#define ESA_FLAG_GATHER_ONLY 1
 
 /* Library version, e.g. 100 for 0.1.0. */
 int esa_version(void);

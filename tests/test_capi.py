@@ -56,7 +56,7 @@ def _problem(esa, **kw):
     base = dict(dtype=esa._lib.DTYPES[__import__("torch").bfloat16], batch=1, num_heads=4,
                 num_kv_heads=2, head_dim=128, attn_length=64, layer_idx=3, num_hidden_layers=8,
                 q_len=16, kv_len=16, kv_offset=0, kv_rows=16, row_offset=0, rows=None,
-                scale=128 ** -0.5, reserved=0)
+                scale=128 ** -0.5, flags=0)
     base.update(kw)
     return esa._lib.EsaProblem(**base)
 

@@ -253,3 +253,31 @@ def test_c3_forward_backward_full_size(esa):
         assert torch.allclose(sv, so, atol=1.0, rtol=2e-2)
         del o, dq, dk, dv, ro, rdq, rdk, rdv
         torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("G,w,L,q_len", [(4, 64, 1000, 1000), (4, 97, 333, 333), (8, 64, 517, 517),
+                                         (2, 64, 700, 700), (2, 65, 130, 130), (4, 64, 50, 50),
+                                         (4, 16, 600, 300), (12, 40, 257, 257)])
+def test_window_tensor_core_path(esa, dtype, G, w, L, q_len):
+    """Layer 0 (a causal window of w keys) runs on the tcgen05 kernel for
+    head_dim 128; it must agree with the CUDA-core gather kernel and with the
+    fp32 oracle, including ragged tails, prefill (q_len < kv_len) and windows
+    longer than the sequence."""
+    g = torch.Generator().manual_seed(G * 1000 + w)
+    Hkv, D = 2, 128
+    Hq = Hkv * G
+    q = randn(1, Hq, q_len, D, dtype=dtype, gen=g)
+    k, v = randn(1, Hkv, L, D, dtype=dtype, gen=g), randn(1, Hkv, L, D, dtype=dtype, gen=g)
+    spec = esa.PatternSpec(0, 8, w)
+    o_tc, lse_tc = esa.ops.forward(q, k, v, spec, D ** -0.5)
+    o_g, lse_g = esa.ops.forward(q, k, v, spec, D ** -0.5, gather_only=True)
+    assert (lse_tc - lse_g).abs().max().item() < 1e-2
+    assert (o_tc.float() - o_g.float()).abs().max().item() < 2e-2
+    idx, mask, _ = pattern.prepared_indices(Hq, w, 0, 8, L, q_len, L)
+    ro, _ = naive.naive_forward(q.float(), k.float(), v.float(), torch.from_numpy(idx).to(DEV),
+                                torch.from_numpy(mask).to(DEV), D ** -0.5, G)
+    assert_close(o_tc, ro, dtype, f"window G{G} w{w} L{L}")
+    lse_ref = naive.lse_rows(q, k, torch.from_numpy(idx).to(DEV), torch.from_numpy(mask).to(DEV),
+                             D ** -0.5, G)
+    assert (lse_tc.double() / 1.4426950408889634 - lse_ref).abs().max().item() < 1e-2
