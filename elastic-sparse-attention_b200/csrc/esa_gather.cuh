@@ -69,7 +69,7 @@ __device__ __forceinline__ void fill_slot_rows(const AttnParams& p, int pos, int
 // warps running together read neighbouring rows of the same K/V head.
 // ---------------------------------------------------------------------------
 template <typename T, int D, int NW>
-__global__ void __launch_bounds__(NW * 32)
+__global__ void __launch_bounds__(NW * 32, 2)
 fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
   using L = Layout<T, D>;
   using V = Vec<T>;
@@ -104,20 +104,24 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
     }
     __syncwarp();
 
-    // Scores (base-2 scaled), one slot per lane per sub-chunk of 32 slots.
+    // Scores (base-2 scaled), one slot per lane per sub-chunk of 32 slots.  All
+    // LPR row loads of a sub-chunk are issued before the first use.
     float mloc = -INFINITY;
     for (int s0 = 0; s0 < wpad; s0 += 32) {
-      float part[LPR];
+      uint4 kb[LPR];
 #pragma unroll
       for (int m = 0; m < LPR; ++m) {
         const int row = sidx[s0 + m * RPW + g];
-        float acc = 0.f;
-        if (row >= 0) {
-          float kf[EPL];
-          V::to_float(ldg16(Kb + (int64_t)row * p.sks), kf);
+        kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
+      }
+      float part[LPR];
 #pragma unroll
-          for (int e = 0; e < EPL; ++e) acc = fmaf(qf[e], kf[e], acc);
-        }
+      for (int m = 0; m < LPR; ++m) {
+        float kf[EPL];
+        V::to_float(kb[m], kf);
+        float acc = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc = fmaf(qf[e], kf[e], acc);
         part[m] = acc;
       }
       transpose_reduce<LPR>(part, lane);
@@ -142,17 +146,19 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
     for (int s0 = 0; s0 < wpad; s0 += 32) {
+      uint4 vb[LPR];
 #pragma unroll
       for (int m = 0; m < LPR; ++m) {
-        const int k = s0 + m * RPW + g;
-        const int row = sidx[k];
-        if (row >= 0) {
-          const float pk = ssc[k];
-          float vf[EPL];
-          V::to_float(ldg16(Vb + (int64_t)row * p.svs), vf);
+        const int row = sidx[s0 + m * RPW + g];
+        vb[m] = row >= 0 ? ldg16(Vb + (int64_t)row * p.svs) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-          for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pk, vf[e], acc[e]);
-        }
+      for (int m = 0; m < LPR; ++m) {
+        const float pk = ssc[s0 + m * RPW + g];   // 0 for masked slots
+        float vf[EPL];
+        V::to_float(vb[m], vf);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pk, vf[e], acc[e]);
       }
     }
 #pragma unroll
@@ -176,7 +182,7 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
 // Same grid and pair order as the forward.
 // ---------------------------------------------------------------------------
 template <typename T, int D, int NW>
-__global__ void __launch_bounds__(NW * 32)
+__global__ void __launch_bounds__(NW * 32, 2)
 bwd_query_kernel(const AttnParams p, int rows_per_cta) {
   using L = Layout<T, D>;
   using V = Vec<T>;
@@ -227,22 +233,39 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
 
     for (int s0 = 0; s0 < wpad; s0 += 32) {
       float ps[LPR], pp[LPR];
+      {
+        uint4 kb[LPR];
 #pragma unroll
-      for (int m = 0; m < LPR; ++m) {
-        const int row = sidx[s0 + m * RPW + g];
-        float a = 0.f, c = 0.f;
-        if (row >= 0) {
-          float kf[EPL], vf[EPL];
-          V::to_float(ldg16(Kb + (int64_t)row * p.sks), kf);
-          V::to_float(ldg16(Vb + (int64_t)row * p.svs), vf);
-#pragma unroll
-          for (int e = 0; e < EPL; ++e) {
-            a = fmaf(qf[e], kf[e], a);
-            c = fmaf(df[e], vf[e], c);
-          }
+        for (int m = 0; m < LPR; ++m) {
+          const int row = sidx[s0 + m * RPW + g];
+          kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
         }
-        ps[m] = a;
-        pp[m] = c;
+#pragma unroll
+        for (int m = 0; m < LPR; ++m) {
+          float kf[EPL];
+          V::to_float(kb[m], kf);
+          float a = 0.f;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) a = fmaf(qf[e], kf[e], a);
+          ps[m] = a;
+        }
+      }
+      {
+        uint4 vb[LPR];
+#pragma unroll
+        for (int m = 0; m < LPR; ++m) {
+          const int row = sidx[s0 + m * RPW + g];
+          vb[m] = row >= 0 ? ldg16(Vb + (int64_t)row * p.svs) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int m = 0; m < LPR; ++m) {
+          float vf[EPL];
+          V::to_float(vb[m], vf);
+          float c = 0.f;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) c = fmaf(df[e], vf[e], c);
+          pp[m] = c;
+        }
       }
       transpose_reduce<LPR>(ps, lane);
       transpose_reduce<LPR>(pp, lane);
@@ -261,17 +284,19 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
     for (int s0 = 0; s0 < wpad; s0 += 32) {
+      uint4 kb[LPR];
 #pragma unroll
       for (int m = 0; m < LPR; ++m) {
-        const int k = s0 + m * RPW + g;
-        const int row = sidx[k];
-        if (row >= 0) {
-          const float dsk = sds[k];
-          float kf[EPL];
-          V::to_float(ldg16(Kb + (int64_t)row * p.sks), kf);
+        const int row = sidx[s0 + m * RPW + g];
+        kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-          for (int e = 0; e < EPL; ++e) acc[e] = fmaf(dsk, kf[e], acc[e]);
-        }
+      for (int m = 0; m < LPR; ++m) {
+        const float dsk = sds[s0 + m * RPW + g];   // 0 for masked slots
+        float kf[EPL];
+        V::to_float(kb[m], kf);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] = fmaf(dsk, kf[e], acc[e]);
       }
     }
 #pragma unroll
@@ -294,7 +319,7 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
 // one writes dK / dV in the input dtype.
 // ---------------------------------------------------------------------------
 template <typename T, int D, int NW, int RW>
-__global__ void __launch_bounds__(NW * 32)
+__global__ void __launch_bounds__(NW * 32, 2)
 bwd_key_kernel(const AttnParams p) {
   using L = Layout<T, D>;
   using V = Vec<T>;
@@ -373,28 +398,54 @@ bwd_key_kernel(const AttnParams p) {
       }
       const int total = __shfl_sync(0xffffffffu, off, 31);
       off -= len;
-      for (int u0 = 0; u0 < total; u0 += RPW) {
-        int owner = 0;
+      for (int u0 = 0; u0 < total; u0 += 32) {
+        // Lane l resolves user u0 + l: owner = the last lane whose run starts
+        // at or before it (zero-length lanes share the next lane's offset).
+        const int u = u0 + lane;
+        int o = 0;
 #pragma unroll
-        for (int gg = 0; gg < RPW; ++gg) {
-          const unsigned bm = __ballot_sync(0xffffffffu, len > 0 && off <= u0 + gg);
-          if (gg == g) owner = bm ? 31 - __clz(bm) : 0;
+        for (int st = 16; st >= 1; st >>= 1) {
+          const int c = o + st;
+          if (__shfl_sync(0xffffffffu, off, c) <= u) o = c;
         }
-        const int o_start = __shfl_sync(0xffffffffu, start, owner);
-        const int o_off = __shfl_sync(0xffffffffu, off, owner);
-        const int u = u0 + g;
+        const int o_start = __shfl_sync(0xffffffffu, start, o);
+        const int o_off = __shfl_sync(0xffffffffu, off, o);
+        int my_qi = 0;
+        float my_p = 0.f, my_ds = 0.f;
         if (u < total) {
           const int jq = o_start + (u - o_off);
-          const int qi = p.row_perm ? (int)p.row_perm[jq] : jq;
-          const int kk = owner + 32 * cc;
-          const float2 pd = pdsb[(int64_t)kk * n + qi];
-          float qf[EPL], df[EPL];
-          V::to_float(ldg16(qbase + (int64_t)qi * p.sqs), qf);
-          V::to_float(ldg16(dbase + (int64_t)qi * p.sdos), df);
+          my_qi = p.row_perm ? (int)p.row_perm[jq] : jq;
+          const float2 pd = pdsb[(int64_t)(o + 32 * cc) * n + my_qi];
+          my_p = pd.x;
+          my_ds = pd.y;
+        }
+        // Users u0 + m*RPW + g (m < LPR) are handled by row group g, in batches
+        // whose q / dO row loads are all issued before use.
+        constexpr int NB = LPR < 4 ? LPR : 4;
 #pragma unroll
-          for (int e = 0; e < EPL; ++e) {
-            adk[e] = fmaf(pd.y, qf[e], adk[e]);
-            adv[e] = fmaf(pd.x, df[e], adv[e]);
+        for (int m0 = 0; m0 < LPR; m0 += NB) {
+          uint4 qb[NB], db[NB];
+          float pb[NB], sb[NB];
+#pragma unroll
+          for (int mb = 0; mb < NB; ++mb) {
+            const int src = (m0 + mb) * RPW + g;
+            const int qi = __shfl_sync(0xffffffffu, my_qi, src);
+            pb[mb] = __shfl_sync(0xffffffffu, my_p, src);
+            sb[mb] = __shfl_sync(0xffffffffu, my_ds, src);
+            const bool valid = u0 + src < total;
+            qb[mb] = valid ? ldg16(qbase + (int64_t)qi * p.sqs) : make_uint4(0, 0, 0, 0);
+            db[mb] = valid ? ldg16(dbase + (int64_t)qi * p.sdos) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int mb = 0; mb < NB; ++mb) {
+            float qf[EPL], df[EPL];
+            V::to_float(qb[mb], qf);
+            V::to_float(db[mb], df);
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+              adk[e] = fmaf(sb[mb], qf[e], adk[e]);
+              adv[e] = fmaf(pb[mb], df[e], adv[e]);
+            }
           }
         }
       }

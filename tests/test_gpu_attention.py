@@ -3,7 +3,11 @@
 
 Tolerances: fp32 inputs within max-abs 1e-4 of
 the fp32 fallback; bf16/fp16 outputs and gradients within max-abs 2e-2 and
-mean-abs 2e-3 of an fp32 fallback run on the same (rounded) inputs.
+mean-abs 2e-3 of an fp32 fallback run on the same (rounded) inputs, where the
+fp32 result is first rounded to the output dtype: an output stored in bf16
+cannot be closer than half a bf16 ulp (0.031 at magnitudes 8..16, which
+layer-0 dK/dV of the first key rows reach), so the bound is applied to the
+error beyond that unavoidable rounding.
 """
 import numpy as np
 import pytest
@@ -42,7 +46,8 @@ def run_oracle(q, k, v, do, layer, nl, w, cache_position=None, chunk=1024):
 
 
 def assert_close(got, want, dtype, what):
-    got, want = got.float(), want.float()
+    want = want.float() if dtype == torch.float32 else want.to(dtype).float()
+    got = got.float()
     err = (got - want).abs()
     if dtype == torch.float32:
         assert err.max().item() <= F32_TOL, (what, err.max().item())
