@@ -3,11 +3,12 @@
 
 Tolerances: fp32 inputs within max-abs 1e-4 of
 the fp32 fallback; bf16/fp16 outputs and gradients within max-abs 2e-2 and
-mean-abs 2e-3 of an fp32 fallback run on the same (rounded) inputs, where the
-fp32 result is first rounded to the output dtype: an output stored in bf16
-cannot be closer than half a bf16 ulp (0.031 at magnitudes 8..16, which
-layer-0 dK/dV of the first key rows reach), so the bound is applied to the
-error beyond that unavoidable rounding.
+mean-abs 2e-3 of an fp32 fallback run on the same (rounded) inputs.  An
+output stored in bf16 cannot be closer to the fp32 value than half a bf16 ulp,
+which exceeds 2e-2 from magnitude 8 up (dK/dV of the first key rows reach
+8..16: at layer 0 query 0 gives key 0 the weight 1, at layer 7 head 0 sends
+all 131072 queries' slot 0 to key 0), so the max-abs bound is 2e-2 plus half
+an ulp of the output dtype at |reference| (2^-8 |ref| for bf16, 2^-11 for fp16).
 """
 import numpy as np
 import pytest
@@ -45,14 +46,18 @@ def run_oracle(q, k, v, do, layer, nl, w, cache_position=None, chunk=1024):
         torch.from_numpy(mask).to(q.device), D ** -0.5, Hq // k.shape[1], chunk=chunk)
 
 
+HALF_ULP = {torch.bfloat16: 2.0 ** -8, torch.float16: 2.0 ** -11}
+
+
 def assert_close(got, want, dtype, what):
-    want = want.float() if dtype == torch.float32 else want.to(dtype).float()
+    want = want.float()
     got = got.float()
     err = (got - want).abs()
     if dtype == torch.float32:
         assert err.max().item() <= F32_TOL, (what, err.max().item())
     else:
-        assert err.max().item() <= LOW_MAX, (what, err.max().item())
+        excess = err - (LOW_MAX + HALF_ULP[dtype] * want.abs())
+        assert excess.max().item() <= 0, (what, err.max().item(), excess.max().item())
         assert err.mean().item() <= LOW_MEAN, (what, err.mean().item())
 
 
