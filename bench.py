@@ -404,8 +404,31 @@ def bench_reference(args, world, rank):
                     "d2h_bytes_per_step": 0}}
 
 
+def profile_case(args):
+    """One forward + backward of one layer at a reduced C3 shape (for ncu)."""
+    import elastic_sparse_attention_b200 as esa
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    n = args.seq_len
+    q = torch.randn(B, HQ, n, D, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, HKV, n, D, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, HKV, n, D, device=dev, generator=g).to(torch.bfloat16)
+    do = torch.randn(B, HQ, n, D, device=dev, generator=g).to(torch.bfloat16)
+    spec = esa.PatternSpec(args.layer, NL, W)
+    for _ in range(args.steps):
+        o, lse = esa.ops.forward(q, k, v, spec, D ** -0.5)
+        esa.ops.backward(q, k, v, o, lse, do, spec, D ** -0.5)
+    torch.cuda.synchronize()
+    print(json.dumps({"case": "one-layer", "seq_len": n, "layer": args.layer,
+                      "out_mean_abs": float(o.float().abs().mean())}))
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", choices=["step", "one-layer"], default="step",
+                    help="one-layer: a single fwd+bwd at --seq-len/--layer, for profilers")
+    ap.add_argument("--seq-len", type=int, default=32768)
+    ap.add_argument("--layer", type=int, default=5)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -413,6 +436,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.case == "one-layer":
+        profile_case(args)
+        return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
