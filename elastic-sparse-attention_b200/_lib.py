@@ -22,7 +22,7 @@ DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 # Every symbol exported by include/esa_b200.h.
 EXPORTED = ("esa_version", "esa_last_error", "esa_pattern", "esa_pattern_audit", "esa_forward",
-            "esa_backward_workspace_size", "esa_backward")
+            "esa_backward_workspace_size", "esa_backward", "esa_backward_noalloc")
 
 
 class EsaTensor(ctypes.Structure):

@@ -433,3 +433,65 @@ int esa_backward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_te
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// esa_backward_noalloc: the backward with its workspace in a fixed array that
+// is part of the library, for callers that cannot allocate device memory (see
+// include/esa_b200.h).  It forwards to esa_backward with that array as the
+// workspace; nothing else about the backward differs.
+// ---------------------------------------------------------------------------
+namespace {
+
+// The workspace itself.  Every GPU on which this library's kernels are loaded
+// holds these ESA_NOALLOC_WORKSPACE_BYTES until the process exits.  Host code
+// must not pass the symbol itself to a kernel (on the host it names a shadow
+// variable, not device memory); it uses the device address looked up below.
+static __device__ __align__(256) unsigned char g_noalloc_workspace[ESA_NOALLOC_WORKSPACE_BYTES];
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[kNoallocMaxDevices] = {};
+
+// Device address of g_noalloc_workspace on the current device, looked up once
+// per device (cudaGetSymbolAddress with that device current) and cached.
+int noalloc_workspace_address(void** out) {
+  int dev = -1;
+  const cudaError_t de = cudaGetDevice(&dev);
+  if (de != cudaSuccess) return fail(ESA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(de));
+  if (dev < 0 || dev >= kNoallocMaxDevices)
+    return fail(ESA_ERR_UNSUPPORTED, "esa_backward_noalloc: device ordinal %d above %d", dev,
+                kNoallocMaxDevices - 1);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_addr[dev]) {
+    void* addr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_workspace);
+    if (e != cudaSuccess || !addr)
+      return fail(ESA_ERR_CUDA, "esa_backward_noalloc: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(e));
+    g_noalloc_addr[dev] = addr;
+  }
+  *out = g_noalloc_addr[dev];
+  return ESA_OK;
+}
+
+}  // namespace
+
+extern "C" int esa_backward_noalloc(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k,
+                                    esa_tensor_t v, esa_tensor_t o, const float* lse,
+                                    esa_tensor_t dout, esa_tensor_t dq, esa_tensor_t dk,
+                                    esa_tensor_t dv, const int64_t* sorted_rows,
+                                    const int64_t* row_perm, void* stream) {
+  if (int rc = check_problem(pb)) return rc;
+  const size_t need = esa_backward_workspace_size(pb);
+  if (need > ESA_NOALLOC_WORKSPACE_BYTES)
+    return fail(ESA_ERR_WORKSPACE,
+                "esa_backward_noalloc: this problem needs %zu bytes of workspace, more than the "
+                "%zu-byte array built into the library; call esa_backward with a workspace",
+                need, (size_t)ESA_NOALLOC_WORKSPACE_BYTES);
+  void* ws = nullptr;
+  if (int rc = noalloc_workspace_address(&ws)) return rc;
+  // Every workspace byte the backward reads is written earlier in the same
+  // call, so the array needs no clearing between calls.
+  return esa_backward(pb, q, k, v, o, lse, dout, dq, dk, dv, sorted_rows, row_perm, ws,
+                      ESA_NOALLOC_WORKSPACE_BYTES, stream);
+}

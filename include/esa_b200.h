@@ -147,6 +147,35 @@ int esa_backward(const esa_problem_t* prob, esa_tensor_t q, esa_tensor_t k, esa_
                  const int64_t* row_perm, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* Size of the workspace array built into the library for esa_backward_noalloc. */
+#define ESA_NOALLOC_WORKSPACE_BYTES (16u * 1024u * 1024u)
+
+/*
+ * esa_backward_noalloc -- esa_backward for callers that cannot allocate device
+ * memory, e.g. a plugin running inside a host application that owns every GPU
+ * allocation, or a serving loop that must not allocate once it is running.
+ * It takes the same arguments as esa_backward minus the workspace, and uses an
+ * array of ESA_NOALLOC_WORKSPACE_BYTES (16 MiB) compiled into the library
+ * instead; it calls no cudaMalloc, cudaFree or other allocating routine.  No
+ * counterpart in the reference (its backward allocates dq/dk/dv with torch).
+ *
+ * Limit: a problem whose esa_backward_workspace_size() exceeds 16 MiB is
+ * rejected with ESA_ERR_WORKSPACE (the workspace is B * num_heads *
+ * attention_length * q_len * 8 bytes, plus 8 * B * num_kv_heads * kv_rows *
+ * head_dim bytes with GQA: e.g. 8 heads, w=64, 2048 query rows fit).
+ * Set-up: the first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current) and caches it; make that
+ * first call before any stream capture.  Call with the tensors' device current.
+ * Sharing: every call on a device uses the same array and leaves its contents
+ * behind; calls that overlap on the GPU (other streams, other threads) race
+ * and corrupt each other's gradients, so serialise them.  Nothing needs
+ * clearing: each call writes every workspace byte before reading it.
+ */
+int esa_backward_noalloc(const esa_problem_t* prob, esa_tensor_t q, esa_tensor_t k,
+                         esa_tensor_t v, esa_tensor_t o, const float* lse, esa_tensor_t dout,
+                         esa_tensor_t dq, esa_tensor_t dk, esa_tensor_t dv,
+                         const int64_t* sorted_rows, const int64_t* row_perm, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
