@@ -317,18 +317,48 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
 // rows; lanes own slot columns k = lane + 32 * cc.  With G > 1 the G launches
 // run in order on one stream and accumulate into the fp32 workspace; the last
 // one writes dK / dV in the input dtype.
+//
+// The q / dO rows of a key row's users are copied with cp.async (16 bytes per
+// lane, L1 bypassed) into a per-warp ring of two shared-memory stages of UB
+// users each, so the warp computes one stage while the next is in flight.
 // ---------------------------------------------------------------------------
+template <typename T, int D>
+struct KeyStage {
+  static constexpr int kRowBytes = D * (int)sizeof(T);
+  static constexpr int kUsers = (4096 / kRowBytes) < 32 ? (4096 / kRowBytes) : 32;  // per stage
+  static constexpr int kStageBytes = kUsers * 2 * kRowBytes;                       // q + dO rows
+  static constexpr int kWarpBytes = 2 * kStageBytes;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src, bool valid) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gmem_src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 template <typename T, int D, int NW, int RW>
-__global__ void __launch_bounds__(NW * 32, 2)
+__global__ void __launch_bounds__(NW * 32, 1)
 bwd_key_kernel(const AttnParams p) {
   using L = Layout<T, D>;
   using V = Vec<T>;
+  using S = KeyStage<T, D>;
   constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  constexpr int UB = S::kUsers;
+  static_assert(UB % RPW == 0 && UB <= 32, "stage size must hold whole warp loads");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int w = p.pat.w;
   const int ncol = (w + 31) >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int* scur = reinterpret_cast<int*>(smem_raw) + warp * ncol * 32;
+  unsigned char* ring = smem_raw + warp * S::kWarpBytes;
+  int* scur = reinterpret_cast<int*>(smem_raw + NW * S::kWarpBytes) + warp * ncol * 32;
   const int g = lane / LPR, r = lane % LPR;
   const int hkv = blockIdx.y, b = blockIdx.z;
   const int h = hkv * p.G + p.head_in_group;
@@ -363,8 +393,12 @@ bwd_key_kernel(const AttnParams p) {
     }
   }
 
-  const T* qbase = reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh + r * EPL;
-  const T* dbase = reinterpret_cast<const T*>(p.dout) + b * p.sdob + h * p.sdoh + r * EPL;
+  const unsigned char* qbase = reinterpret_cast<const unsigned char*>(
+      reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh);
+  const unsigned char* dbase = reinterpret_cast<const unsigned char*>(
+      reinterpret_cast<const T*>(p.dout) + b * p.sdob + h * p.sdoh);
+  const int64_t qrow_bytes = p.sqs * (int64_t)sizeof(T);
+  const int64_t drow_bytes = p.sdos * (int64_t)sizeof(T);
   const float2* pdsb = p.pds + (int64_t)(b * p.Hq + h) * w * n;
 
   for (int lr = lr0; lr < lr1; ++lr) {
@@ -398,56 +432,75 @@ bwd_key_kernel(const AttnParams p) {
       }
       const int total = __shfl_sync(0xffffffffu, off, 31);
       off -= len;
-      for (int u0 = 0; u0 < total; u0 += 32) {
-        // Lane l resolves user u0 + l: owner = the last lane whose run starts
-        // at or before it (zero-length lanes share the next lane's offset).
+      if (total == 0) continue;
+
+      // Resolve users u0 + lane (lane < UB) and start their row copies into
+      // stage `st`; returns this lane's (p, dS) of its user (0 when none).
+      auto issue = [&](int u0, int st, float& my_p, float& my_ds) {
         const int u = u0 + lane;
         int o = 0;
 #pragma unroll
-        for (int st = 16; st >= 1; st >>= 1) {
-          const int c = o + st;
+        for (int sh = 16; sh >= 1; sh >>= 1) {
+          const int c = o + sh;
           if (__shfl_sync(0xffffffffu, off, c) <= u) o = c;
         }
         const int o_start = __shfl_sync(0xffffffffu, start, o);
         const int o_off = __shfl_sync(0xffffffffu, off, o);
         int my_qi = 0;
-        float my_p = 0.f, my_ds = 0.f;
-        if (u < total) {
+        my_p = 0.f;
+        my_ds = 0.f;
+        if (lane < UB && u < total) {
           const int jq = o_start + (u - o_off);
           my_qi = p.row_perm ? (int)p.row_perm[jq] : jq;
           const float2 pd = pdsb[(int64_t)(o + 32 * cc) * n + my_qi];
           my_p = pd.x;
           my_ds = pd.y;
         }
-        // Users u0 + m*RPW + g (m < LPR) are handled by row group g, in batches
-        // whose q / dO row loads are all issued before use.
-        constexpr int NB = LPR < 4 ? LPR : 4;
+        unsigned char* stage = ring + st * S::kStageBytes;
 #pragma unroll
-        for (int m0 = 0; m0 < LPR; m0 += NB) {
-          uint4 qb[NB], db[NB];
-          float pb[NB], sb[NB];
+        for (int m = 0; m < UB / RPW; ++m) {
+          const int x = m * RPW + g;   // user slot in the stage
+          const int qi = __shfl_sync(0xffffffffu, my_qi, x);
+          const bool valid = u0 + x < total;
+          unsigned char* dst = stage + x * 2 * S::kRowBytes + r * 16;
+          cp_async16(dst, qbase + qi * qrow_bytes + r * 16, valid);
+          cp_async16(dst + S::kRowBytes, dbase + qi * drow_bytes + r * 16, valid);
+        }
+        cp_async_commit();
+      };
+
+      float p_cur, s_cur, p_nxt = 0.f, s_nxt = 0.f;
+      issue(0, 0, p_cur, s_cur);
+      int st = 0;
+      for (int u0 = 0; u0 < total; u0 += UB) {
+        const bool more = u0 + UB < total;
+        if (more) {
+          issue(u0 + UB, st ^ 1, p_nxt, s_nxt);
+          cp_async_wait<1>();
+        } else {
+          cp_async_wait<0>();
+        }
+        __syncwarp();
+        const unsigned char* stage = ring + st * S::kStageBytes;
 #pragma unroll
-          for (int mb = 0; mb < NB; ++mb) {
-            const int src = (m0 + mb) * RPW + g;
-            const int qi = __shfl_sync(0xffffffffu, my_qi, src);
-            pb[mb] = __shfl_sync(0xffffffffu, my_p, src);
-            sb[mb] = __shfl_sync(0xffffffffu, my_ds, src);
-            const bool valid = u0 + src < total;
-            qb[mb] = valid ? ldg16(qbase + (int64_t)qi * p.sqs) : make_uint4(0, 0, 0, 0);
-            db[mb] = valid ? ldg16(dbase + (int64_t)qi * p.sdos) : make_uint4(0, 0, 0, 0);
-          }
+        for (int m = 0; m < UB / RPW; ++m) {
+          const int x = m * RPW + g;
+          const float pm = __shfl_sync(0xffffffffu, p_cur, x);
+          const float sm = __shfl_sync(0xffffffffu, s_cur, x);
+          const unsigned char* src = stage + x * 2 * S::kRowBytes + r * 16;
+          float qf[EPL], df[EPL];
+          V::to_float(*reinterpret_cast<const uint4*>(src), qf);
+          V::to_float(*reinterpret_cast<const uint4*>(src + S::kRowBytes), df);
 #pragma unroll
-          for (int mb = 0; mb < NB; ++mb) {
-            float qf[EPL], df[EPL];
-            V::to_float(qb[mb], qf);
-            V::to_float(db[mb], df);
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) {
-              adk[e] = fmaf(sb[mb], qf[e], adk[e]);
-              adv[e] = fmaf(pb[mb], df[e], adv[e]);
-            }
+          for (int e = 0; e < EPL; ++e) {
+            adk[e] = fmaf(sm, qf[e], adk[e]);
+            adv[e] = fmaf(pm, df[e], adv[e]);
           }
         }
+        __syncwarp();   // every lane is done with this stage before it is refilled
+        p_cur = p_nxt;
+        s_cur = s_nxt;
+        st ^= 1;
       }
     }
 #pragma unroll
