@@ -226,7 +226,7 @@ int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
   }
   const int rpc = rows_per_cta(p.G);
   const int wpad = (p.pat.w + 31) & ~31;
-  const size_t smem = (size_t)kFwdWarps * 2 * wpad * sizeof(int);
+  const size_t smem = (size_t)kFwdWarps * 3 * wpad * sizeof(int);
   auto kern = esa::fwd_gather_kernel<T, D, kFwdWarps>;
   if (int rc = prepare_smem(kern, smem)) return rc;
   dim3 grid((p.n_rows + rpc - 1) / rpc, p.Hkv, p.B);
@@ -239,7 +239,7 @@ int launch_backward(const esa::AttnParams& p, cudaStream_t s) {
   if (p.n_rows > 0) {
     const int rpc = rows_per_cta(p.G);
     const int wpad = (p.pat.w + 31) & ~31;
-    const size_t smem = (size_t)kFwdWarps * 2 * wpad * sizeof(int);
+    const size_t smem = (size_t)kFwdWarps * 3 * wpad * sizeof(int);
     auto kern = esa::bwd_query_kernel<T, D, kFwdWarps>;
     if (int rc = prepare_smem(kern, smem)) return rc;
     dim3 grid((p.n_rows + rpc - 1) / rpc, p.Hkv, p.B);

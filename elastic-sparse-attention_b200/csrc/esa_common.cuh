@@ -121,6 +121,105 @@ template <> struct Vec<__half> {
   }
 };
 
+// ---------------------------------------------------------------------------
+// Arithmetic on one 16-byte vector with fp32 accumulation.  For bf16 / fp16
+// data the products use the mixed-precision FMA (16-bit x 16-bit + fp32 ->
+// fp32, full rate on sm_100), so no conversion instructions are issued; for
+// fp32 data it is plain FFMA.
+//   dot(a, b, acc)      -> acc + sum_e a[e] * b[e]
+//   axpy(s, b, acc[])   -> acc[e] += s * b[e]   (s as from scalar(): rounded
+//                          to the vector's type for 16-bit data)
+// ---------------------------------------------------------------------------
+template <typename T> struct Mix;
+
+template <> struct Mix<float> {
+  using Scalar = float;
+  __device__ __forceinline__ static Scalar scalar(float s) { return s; }
+  __device__ __forceinline__ static float to_float(Scalar s) { return s; }
+  __device__ __forceinline__ static float dot(const uint4& a, const uint4& b, float acc) {
+    acc = fmaf(__uint_as_float(a.x), __uint_as_float(b.x), acc);
+    acc = fmaf(__uint_as_float(a.y), __uint_as_float(b.y), acc);
+    acc = fmaf(__uint_as_float(a.z), __uint_as_float(b.z), acc);
+    acc = fmaf(__uint_as_float(a.w), __uint_as_float(b.w), acc);
+    return acc;
+  }
+  __device__ __forceinline__ static void axpy(Scalar s, const uint4& b, float* acc) {
+    acc[0] = fmaf(s, __uint_as_float(b.x), acc[0]);
+    acc[1] = fmaf(s, __uint_as_float(b.y), acc[1]);
+    acc[2] = fmaf(s, __uint_as_float(b.z), acc[2]);
+    acc[3] = fmaf(s, __uint_as_float(b.w), acc[3]);
+  }
+};
+
+#define ESA_MIX16(NAME, PTXTYPE)                                                                  \
+  __device__ __forceinline__ void NAME##_fma2(uint32_t a, uint32_t b, float& c0, float& c1) {     \
+    asm("{\n\t.reg .b16 a0, a1, b0, b1;\n\t"                                                      \
+        "mov.b32 {a0, a1}, %2;\n\tmov.b32 {b0, b1}, %3;\n\t"                                     \
+        "fma.rn.f32." PTXTYPE " %0, a0, b0, %0;\n\t"                                             \
+        "fma.rn.f32." PTXTYPE " %1, a1, b1, %1;\n\t}"                                            \
+        : "+f"(c0), "+f"(c1)                                                                      \
+        : "r"(a), "r"(b));                                                                        \
+  }                                                                                               \
+  __device__ __forceinline__ void NAME##_axpy2(uint16_t s, uint32_t b, float& c0, float& c1) {    \
+    asm("{\n\t.reg .b16 b0, b1;\n\t"                                                            \
+        "mov.b32 {b0, b1}, %3;\n\t"                                                               \
+        "fma.rn.f32." PTXTYPE " %0, %2, b0, %0;\n\t"                                             \
+        "fma.rn.f32." PTXTYPE " %1, %2, b1, %1;\n\t}"                                            \
+        : "+f"(c0), "+f"(c1)                                                                      \
+        : "h"(s), "r"(b));                                                                        \
+  }
+ESA_MIX16(bf16, "bf16")
+ESA_MIX16(f16, "f16")
+#undef ESA_MIX16
+
+template <> struct Mix<__nv_bfloat16> {
+  using Scalar = uint16_t;
+  __device__ __forceinline__ static Scalar scalar(float s) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(s));
+  }
+  __device__ __forceinline__ static float to_float(Scalar s) {
+    return __uint_as_float(static_cast<uint32_t>(s) << 16);
+  }
+  __device__ __forceinline__ static float dot(const uint4& a, const uint4& b, float acc) {
+    float c1 = 0.f;
+    bf16_fma2(a.x, b.x, acc, c1);
+    bf16_fma2(a.y, b.y, acc, c1);
+    bf16_fma2(a.z, b.z, acc, c1);
+    bf16_fma2(a.w, b.w, acc, c1);
+    return acc + c1;
+  }
+  __device__ __forceinline__ static void axpy(Scalar s, const uint4& b, float* acc) {
+    bf16_axpy2(s, b.x, acc[0], acc[1]);
+    bf16_axpy2(s, b.y, acc[2], acc[3]);
+    bf16_axpy2(s, b.z, acc[4], acc[5]);
+    bf16_axpy2(s, b.w, acc[6], acc[7]);
+  }
+};
+
+template <> struct Mix<__half> {
+  using Scalar = uint16_t;
+  __device__ __forceinline__ static Scalar scalar(float s) {
+    return __half_as_ushort(__float2half_rn(s));
+  }
+  __device__ __forceinline__ static float to_float(Scalar s) {
+    return __half2float(__ushort_as_half(s));
+  }
+  __device__ __forceinline__ static float dot(const uint4& a, const uint4& b, float acc) {
+    float c1 = 0.f;
+    f16_fma2(a.x, b.x, acc, c1);
+    f16_fma2(a.y, b.y, acc, c1);
+    f16_fma2(a.z, b.z, acc, c1);
+    f16_fma2(a.w, b.w, acc, c1);
+    return acc + c1;
+  }
+  __device__ __forceinline__ static void axpy(Scalar s, const uint4& b, float* acc) {
+    f16_axpy2(s, b.x, acc[0], acc[1]);
+    f16_axpy2(s, b.y, acc[2], acc[3]);
+    f16_axpy2(s, b.z, acc[4], acc[5]);
+    f16_axpy2(s, b.w, acc[6], acc[7]);
+  }
+};
+
 __device__ __forceinline__ uint4 ldg16(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }

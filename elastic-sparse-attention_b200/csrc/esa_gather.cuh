@@ -73,13 +73,16 @@ __global__ void __launch_bounds__(NW * 32, 2)
 fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
   using L = Layout<T, D>;
   using V = Vec<T>;
+  using M = Mix<T>;
+  using Sc = typename M::Scalar;
   constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int w = p.pat.w;
   const int wpad = (w + 31) & ~31;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int* sidx = reinterpret_cast<int*>(smem_raw) + warp * 2 * wpad;
+  int* sidx = reinterpret_cast<int*>(smem_raw) + warp * 3 * wpad;
   float* ssc = reinterpret_cast<float*>(sidx + wpad);
+  Sc* sps = reinterpret_cast<Sc*>(ssc + wpad);    // softmax weights in the input type
   const int g = lane / LPR, r = lane % LPR;
   const int hkv = blockIdx.y, b = blockIdx.z;
   const int row0 = blockIdx.x * rows_per_cta;
@@ -94,14 +97,8 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
     const int pos = query_pos(p, j);
     fill_slot_rows(p, pos, h, wpad, lane, sidx);
 
-    float qf[EPL];
-    {
-      const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh +
-                      (int64_t)j * p.sqs + r * EPL;
-      V::to_float(ldg16_stream(qrow), qf);
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) qf[e] *= p.scale_log2;
-    }
+    const uint4 qv = ldg16_stream(reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh +
+                                  (int64_t)j * p.sqs + r * EPL);
     __syncwarp();
 
     // Scores (base-2 scaled), one slot per lane per sub-chunk of 32 slots.  All
@@ -116,28 +113,23 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
       }
       float part[LPR];
 #pragma unroll
-      for (int m = 0; m < LPR; ++m) {
-        float kf[EPL];
-        V::to_float(kb[m], kf);
-        float acc = 0.f;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) acc = fmaf(qf[e], kf[e], acc);
-        part[m] = acc;
-      }
+      for (int m = 0; m < LPR; ++m) part[m] = M::dot(qv, kb[m], 0.f);
       transpose_reduce<LPR>(part, lane);
       const int k = s0 + r * RPW + g;
-      const float s = sidx[k] >= 0 ? part[0] : -INFINITY;
+      const float s = sidx[k] >= 0 ? part[0] * p.scale_log2 : -INFINITY;
       ssc[k] = s;
       mloc = fmaxf(mloc, s);
     }
     float mx = warp_max(mloc);
     mx = mx == -INFINITY ? 0.f : mx;
     __syncwarp();
+    // Weights rounded to the input type once; the normaliser sums the rounded
+    // values so that they add up to one exactly as used.
     float lsum = 0.f;
     for (int k = lane; k < wpad; k += 32) {
-      const float e = exp2f(ssc[k] - mx);
-      ssc[k] = e;
-      lsum += e;
+      const Sc e = M::scalar(exp2f(ssc[k] - mx));
+      sps[k] = e;
+      lsum += M::to_float(e);
     }
     const float l = warp_sum(lsum);
     __syncwarp();
@@ -153,13 +145,7 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
         vb[m] = row >= 0 ? ldg16(Vb + (int64_t)row * p.svs) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int m = 0; m < LPR; ++m) {
-        const float pk = ssc[s0 + m * RPW + g];   // 0 for masked slots
-        float vf[EPL];
-        V::to_float(vb[m], vf);
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pk, vf[e], acc[e]);
-      }
+      for (int m = 0; m < LPR; ++m) M::axpy(sps[s0 + m * RPW + g], vb[m], acc);   // 0 when masked
     }
 #pragma unroll
     for (int o = LPR; o < 32; o <<= 1)
@@ -186,13 +172,15 @@ __global__ void __launch_bounds__(NW * 32, 2)
 bwd_query_kernel(const AttnParams p, int rows_per_cta) {
   using L = Layout<T, D>;
   using V = Vec<T>;
+  using M = Mix<T>;
+  using Sc = typename M::Scalar;
   constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int w = p.pat.w;
   const int wpad = (w + 31) & ~31;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int* sidx = reinterpret_cast<int*>(smem_raw) + warp * 2 * wpad;
-  float* sds = reinterpret_cast<float*>(sidx + wpad);
+  int* sidx = reinterpret_cast<int*>(smem_raw) + warp * 3 * wpad;
+  Sc* sds = reinterpret_cast<Sc*>(sidx + wpad);   // dS * scale in the input type
   const int g = lane / LPR, r = lane % LPR;
   const int hkv = blockIdx.y, b = blockIdx.z;
   const int row0 = blockIdx.x * rows_per_cta;
@@ -208,24 +196,17 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
     const int pos = query_pos(p, j);
     fill_slot_rows(p, pos, h, wpad, lane, sidx);
 
-    float qf[EPL], df[EPL];
+    uint4 qv, dv;
     float delta;
     {
       const int64_t jr = (int64_t)j;
       const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh + jr * p.sqs + r * EPL;
       const T* drow = reinterpret_cast<const T*>(p.dout) + b * p.sdob + h * p.sdoh + jr * p.sdos + r * EPL;
       const T* orow = reinterpret_cast<const T*>(p.o) + b * p.sob + h * p.soh + jr * p.sos + r * EPL;
-      float of[EPL];
-      V::to_float(ldg16_stream(qrow), qf);
-      V::to_float(ldg16_stream(drow), df);
-      V::to_float(ldg16_stream(orow), of);
-      float dd = 0.f;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        qf[e] *= p.scale_log2;
-        dd = fmaf(df[e], of[e], dd);
-      }
-      delta = group_allreduce_sum<LPR>(dd);   // rowsum(dO * O), every group holds it
+      qv = ldg16_stream(qrow);
+      dv = ldg16_stream(drow);
+      // rowsum(dO * O), every group holds it
+      delta = group_allreduce_sum<LPR>(M::dot(dv, ldg16_stream(orow), 0.f));
     }
     const float lse2 = p.lse[((int64_t)b * p.Hq + h) * n + j];
     float2* pds_row = p.pds + ((int64_t)(b * p.Hq + h) * w) * n + j;
@@ -241,14 +222,7 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
           kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
-        for (int m = 0; m < LPR; ++m) {
-          float kf[EPL];
-          V::to_float(kb[m], kf);
-          float a = 0.f;
-#pragma unroll
-          for (int e = 0; e < EPL; ++e) a = fmaf(qf[e], kf[e], a);
-          ps[m] = a;
-        }
+        for (int m = 0; m < LPR; ++m) ps[m] = M::dot(qv, kb[m], 0.f);
       }
       {
         uint4 vb[LPR];
@@ -258,25 +232,18 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
           vb[m] = row >= 0 ? ldg16(Vb + (int64_t)row * p.svs) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
-        for (int m = 0; m < LPR; ++m) {
-          float vf[EPL];
-          V::to_float(vb[m], vf);
-          float c = 0.f;
-#pragma unroll
-          for (int e = 0; e < EPL; ++e) c = fmaf(df[e], vf[e], c);
-          pp[m] = c;
-        }
+        for (int m = 0; m < LPR; ++m) pp[m] = M::dot(dv, vb[m], 0.f);
       }
       transpose_reduce<LPR>(ps, lane);
       transpose_reduce<LPR>(pp, lane);
       const int k = s0 + r * RPW + g;
       float pk = 0.f, dsk = 0.f;
       if (sidx[k] >= 0) {
-        pk = exp2f(ps[0] - lse2);
+        pk = exp2f(ps[0] * p.scale_log2 - lse2);
         dsk = pk * (pp[0] - delta) * p.scale;
       }
       if (k < w) pds_row[(int64_t)k * n] = make_float2(pk, dsk);
-      sds[k] = dsk;
+      sds[k] = M::scalar(dsk);
     }
     __syncwarp();
 
@@ -291,13 +258,7 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
         kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int m = 0; m < LPR; ++m) {
-        const float dsk = sds[s0 + m * RPW + g];   // 0 for masked slots
-        float kf[EPL];
-        V::to_float(kb[m], kf);
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[e] = fmaf(dsk, kf[e], acc[e]);
-      }
+      for (int m = 0; m < LPR; ++m) M::axpy(sds[s0 + m * RPW + g], kb[m], acc);   // 0 when masked
     }
 #pragma unroll
     for (int o = LPR; o < 32; o <<= 1)
@@ -349,6 +310,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
 bwd_key_kernel(const AttnParams p) {
   using L = Layout<T, D>;
   using V = Vec<T>;
+  using M = Mix<T>;
+  using Sc = typename M::Scalar;
   using S = KeyStage<T, D>;
   constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
   constexpr int UB = S::kUsers;
@@ -435,8 +398,9 @@ bwd_key_kernel(const AttnParams p) {
       if (total == 0) continue;
 
       // Resolve users u0 + lane (lane < UB) and start their row copies into
-      // stage `st`; returns this lane's (p, dS) of its user (0 when none).
-      auto issue = [&](int u0, int st, float& my_p, float& my_ds) {
+      // stage `st`; returns this lane's (p, dS) of its user (0 when none), in
+      // the input type for 16-bit data.
+      auto issue = [&](int u0, int st, Sc& my_p, Sc& my_ds) {
         const int u = u0 + lane;
         int o = 0;
 #pragma unroll
@@ -447,14 +411,14 @@ bwd_key_kernel(const AttnParams p) {
         const int o_start = __shfl_sync(0xffffffffu, start, o);
         const int o_off = __shfl_sync(0xffffffffu, off, o);
         int my_qi = 0;
-        my_p = 0.f;
-        my_ds = 0.f;
+        my_p = M::scalar(0.f);
+        my_ds = M::scalar(0.f);
         if (lane < UB && u < total) {
           const int jq = o_start + (u - o_off);
           my_qi = p.row_perm ? (int)p.row_perm[jq] : jq;
           const float2 pd = pdsb[(int64_t)(o + 32 * cc) * n + my_qi];
-          my_p = pd.x;
-          my_ds = pd.y;
+          my_p = M::scalar(pd.x);
+          my_ds = M::scalar(pd.y);
         }
         unsigned char* stage = ring + st * S::kStageBytes;
 #pragma unroll
@@ -469,7 +433,7 @@ bwd_key_kernel(const AttnParams p) {
         cp_async_commit();
       };
 
-      float p_cur, s_cur, p_nxt = 0.f, s_nxt = 0.f;
+      Sc p_cur, s_cur, p_nxt = M::scalar(0.f), s_nxt = M::scalar(0.f);
       issue(0, 0, p_cur, s_cur);
       int st = 0;
       for (int u0 = 0; u0 < total; u0 += UB) {
@@ -485,17 +449,11 @@ bwd_key_kernel(const AttnParams p) {
 #pragma unroll
         for (int m = 0; m < UB / RPW; ++m) {
           const int x = m * RPW + g;
-          const float pm = __shfl_sync(0xffffffffu, p_cur, x);
-          const float sm = __shfl_sync(0xffffffffu, s_cur, x);
+          const Sc pm = __shfl_sync(0xffffffffu, p_cur, x);
+          const Sc sm = __shfl_sync(0xffffffffu, s_cur, x);
           const unsigned char* src = stage + x * 2 * S::kRowBytes + r * 16;
-          float qf[EPL], df[EPL];
-          V::to_float(*reinterpret_cast<const uint4*>(src), qf);
-          V::to_float(*reinterpret_cast<const uint4*>(src + S::kRowBytes), df);
-#pragma unroll
-          for (int e = 0; e < EPL; ++e) {
-            adk[e] = fmaf(sm, qf[e], adk[e]);
-            adv[e] = fmaf(pm, df[e], adv[e]);
-          }
+          M::axpy(sm, *reinterpret_cast<const uint4*>(src), adk);
+          M::axpy(pm, *reinterpret_cast<const uint4*>(src + S::kRowBytes), adv);
         }
         __syncwarp();   // every lane is done with this stage before it is refilled
         p_cur = p_nxt;
