@@ -220,6 +220,31 @@ template <> struct Mix<__half> {
   }
 };
 
+// acc[e] += s * b[e] with s in fp32 and the 16-byte vector b converted to
+// fp32 (exact for every input type); for 16-bit data the products use the
+// packed fma.rn.f32x2 (two lanes per instruction).  Used where many terms
+// are summed (the key side of the backward), so s keeps full precision.
+__device__ __forceinline__ void ffma2(float& c0, float& c1, float a0, float a1, float b0,
+                                      float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%0, %1};\n\t"
+      "fma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+template <typename T>
+__device__ __forceinline__ void axpy_f32(float s, const uint4& b, float* acc) {
+  if constexpr (sizeof(T) == 4) {
+    Mix<float>::axpy(s, b, acc);
+  } else {
+    float f[8];
+    Vec<T>::to_float(b, f);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) ffma2(acc[e], acc[e + 1], s, s, f[e], f[e + 1]);
+  }
+}
+
 __device__ __forceinline__ uint4 ldg16(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }

@@ -310,8 +310,6 @@ __global__ void __launch_bounds__(NW * 32, 1)
 bwd_key_kernel(const AttnParams p) {
   using L = Layout<T, D>;
   using V = Vec<T>;
-  using M = Mix<T>;
-  using Sc = typename M::Scalar;
   using S = KeyStage<T, D>;
   constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
   constexpr int UB = S::kUsers;
@@ -398,9 +396,10 @@ bwd_key_kernel(const AttnParams p) {
       if (total == 0) continue;
 
       // Resolve users u0 + lane (lane < UB) and start their row copies into
-      // stage `st`; returns this lane's (p, dS) of its user (0 when none), in
-      // the input type for 16-bit data.
-      auto issue = [&](int u0, int st, Sc& my_p, Sc& my_ds) {
+      // stage `st`; returns this lane's (p, dS) of its user (0 when none).
+      // They stay fp32: a key row can have ~1e5 users (alpha = 1, head 0,
+      // slot 0 sends every query to key 0), too many to sum rounded terms.
+      auto issue = [&](int u0, int st, float& my_p, float& my_ds) {
         const int u = u0 + lane;
         int o = 0;
 #pragma unroll
@@ -411,14 +410,14 @@ bwd_key_kernel(const AttnParams p) {
         const int o_start = __shfl_sync(0xffffffffu, start, o);
         const int o_off = __shfl_sync(0xffffffffu, off, o);
         int my_qi = 0;
-        my_p = M::scalar(0.f);
-        my_ds = M::scalar(0.f);
+        my_p = 0.f;
+        my_ds = 0.f;
         if (lane < UB && u < total) {
           const int jq = o_start + (u - o_off);
           my_qi = p.row_perm ? (int)p.row_perm[jq] : jq;
           const float2 pd = pdsb[(int64_t)(o + 32 * cc) * n + my_qi];
-          my_p = M::scalar(pd.x);
-          my_ds = M::scalar(pd.y);
+          my_p = pd.x;
+          my_ds = pd.y;
         }
         unsigned char* stage = ring + st * S::kStageBytes;
 #pragma unroll
@@ -433,7 +432,7 @@ bwd_key_kernel(const AttnParams p) {
         cp_async_commit();
       };
 
-      Sc p_cur, s_cur, p_nxt = M::scalar(0.f), s_nxt = M::scalar(0.f);
+      float p_cur, s_cur, p_nxt = 0.f, s_nxt = 0.f;
       issue(0, 0, p_cur, s_cur);
       int st = 0;
       for (int u0 = 0; u0 < total; u0 += UB) {
@@ -449,11 +448,11 @@ bwd_key_kernel(const AttnParams p) {
 #pragma unroll
         for (int m = 0; m < UB / RPW; ++m) {
           const int x = m * RPW + g;
-          const Sc pm = __shfl_sync(0xffffffffu, p_cur, x);
-          const Sc sm = __shfl_sync(0xffffffffu, s_cur, x);
+          const float pm = __shfl_sync(0xffffffffu, p_cur, x);
+          const float sm = __shfl_sync(0xffffffffu, s_cur, x);
           const unsigned char* src = stage + x * 2 * S::kRowBytes + r * 16;
-          M::axpy(sm, *reinterpret_cast<const uint4*>(src), adk);
-          M::axpy(pm, *reinterpret_cast<const uint4*>(src + S::kRowBytes), adv);
+          axpy_f32<T>(sm, *reinterpret_cast<const uint4*>(src), adk);
+          axpy_f32<T>(pm, *reinterpret_cast<const uint4*>(src + S::kRowBytes), adv);
         }
         __syncwarp();   // every lane is done with this stage before it is refilled
         p_cur = p_nxt;
