@@ -224,6 +224,18 @@ int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
     if (ht == 4) return launch_window<T, 4>(p, s);
     if (ht == 2) return launch_window<T, 2>(p, s);
   }
+  if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
+    // slot-major tile kernel: 128 pairs per CTA share their K/V rows through L1
+    if (p.pat.w <= esa::kTileMaxW && p.G <= esa::kTilePairs && esa::kTilePairs % p.G == 0 &&
+        !p.rows && p.n_rows >= 256 && !(p.flags & ESA_FLAG_GATHER_ONLY)) {
+      const int tq = esa::kTilePairs / p.G;
+      dim3 grid((p.n_rows + tq - 1) / tq, p.Hkv, p.B);
+      auto kern = esa::fwd_tile_kernel<T, D>;
+      if (int rc = prepare_smem(kern, esa::kTileSmemBytes)) return rc;
+      kern<<<grid, 256, esa::kTileSmemBytes, s>>>(p);
+      return check_launch("forward (tile)");
+    }
+  }
   const int rpc = rows_per_cta(p.G);
   const int wpad = (p.pat.w + 31) & ~31;
   const size_t smem = (size_t)kFwdWarps * 3 * wpad * sizeof(int);

@@ -164,6 +164,185 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
 }
 
 // ---------------------------------------------------------------------------
+// Forward, slot-major tile variant (16-bit types, w <= 64, G divides 128).
+//
+// A CTA owns a tile of 128 (query, head) pairs of one KV head: 128/G
+// consecutive queries x the G heads.  Warp w owns pairs [16w, 16w + 16); half
+// of a warp load serves one pair (RPW = 2 for D = 128).  Unlike
+// fwd_gather_kernel, all warps walk the slots together (two slots per
+// butterfly), so at any moment the CTA reads the K (then V) rows of the same
+// few slots for all 128 pairs: the rows several pairs share (neighbouring
+// queries at small dilation, neighbouring heads at any dilation) are served
+// from L1 after the first miss.  Scores stay in registers (one pair's 64
+// scores live in two lanes), softmax weights go to shared memory in the input
+// type, and each half-warp writes its pair's output row without a reduction.
+// ---------------------------------------------------------------------------
+constexpr int kTilePairs = 128;
+constexpr int kTileMaxW = 64;
+constexpr int kTileSidxBytes = kTilePairs * kTileMaxW * 4;
+constexpr int kTileSmemBytes = 2 * kTileSidxBytes + kTilePairs * 4;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(256, 2)
+fwd_tile_kernel(const AttnParams p) {
+  using L = Layout<T, D>;
+  using V = Vec<T>;
+  using M = Mix<T>;
+  using Sc = typename M::Scalar;
+  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  constexpr int PPW = kTilePairs / 8;      // pairs per warp
+  constexpr int MI = PPW / RPW;            // warp loads per slot
+  static_assert(MI * 2 == LPR, "two slots per transpose-reduce");
+  constexpr int HALF = kTileMaxW / 2;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int(*sidx)[kTileMaxW] = reinterpret_cast<int(*)[kTileMaxW]>(smem_raw);
+  // fp32 scores; after the softmax the same bytes hold the weights in the
+  // input type, laid out as Sc[kTilePairs][kTileMaxW]
+  float(*sbuf)[kTileMaxW] = reinterpret_cast<float(*)[kTileMaxW]>(smem_raw + kTileSidxBytes);
+  Sc(*sp)[kTileMaxW] = reinterpret_cast<Sc(*)[kTileMaxW]>(&sbuf[0][0]);
+  float* sl = reinterpret_cast<float*>(smem_raw + 2 * kTileSidxBytes);
+  const int w = p.pat.w;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane / LPR, r = lane % LPR;
+  const int G = p.G;
+  const int TQ = kTilePairs / G;
+  const int hkv = blockIdx.y, b = blockIdx.z;
+  const int j0 = blockIdx.x * TQ;
+
+  // ---- indices: thread t fills pair t / 2, slots [(t & 1) * 32, +32) ------
+  {
+    const int pi = threadIdx.x >> 1;
+    const int j = j0 + pi / G;
+    const int h = hkv * G + pi % G;
+    const int kbeg = (threadIdx.x & 1) * HALF;
+    if (j < p.n_rows) {
+      const int pos = query_pos(p, j);
+      const RowWin rw = row_window(p.pat, pos);
+      const float t = head_weight(p.pat, h);
+      const float omt = __fsub_rn(1.f, t);
+      for (int k = kbeg; k < kbeg + HALF; ++k) {
+        int row = -1;
+        if (k < w) {
+          const int raw = raw_index(rw, k, t, omt);
+          if (raw <= pos) {
+            row = min(raw, p.kv_len - 1) - p.kv_offset;
+            if (row < 0 || row >= p.kv_rows) {
+              if (p.err) atomicOr(p.err, kErrKvRange);
+              row = -1;
+            }
+          }
+        }
+        sidx[pi][k] = row;
+      }
+    } else {
+      for (int k = kbeg; k < kbeg + HALF; ++k) sidx[pi][k] = -1;
+    }
+  }
+  __syncthreads();
+
+  const int pw0 = warp * PPW;   // first pair of this warp
+  const T* Kb = reinterpret_cast<const T*>(p.k) + b * p.skb + hkv * p.skh + r * EPL;
+  const T* Vb = reinterpret_cast<const T*>(p.v) + b * p.svb + hkv * p.svh + r * EPL;
+
+  {
+    // q chunks of this lane's pairs (pair pw0 + m * RPW + g, m < MI)
+    uint4 qv[MI];
+#pragma unroll
+    for (int m = 0; m < MI; ++m) {
+      const int pi = pw0 + m * RPW + g;
+      const int j = j0 + pi / G;
+      const int h = hkv * G + pi % G;
+      qv[m] = j < p.n_rows ? ldg16_stream(reinterpret_cast<const T*>(p.q) + b * p.sqb +
+                                          h * p.sqh + (int64_t)j * p.sqs + r * EPL)
+                           : make_uint4(0, 0, 0, 0);
+    }
+    // ---- scores, two slots per butterfly: lane r ends with slot k0 + r / MI
+    // of pair pw0 + (r % MI) * RPW + g --------------------------------------
+    const int my_pi = pw0 + (r % MI) * RPW + g;
+    for (int k0 = 0; k0 < w; k0 += 2) {
+      float part[LPR];
+#pragma unroll
+      for (int s2 = 0; s2 < 2; ++s2) {
+        uint4 kb[MI];
+#pragma unroll
+        for (int m = 0; m < MI; ++m) {
+          const int row = sidx[pw0 + m * RPW + g][k0 + s2];
+          kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(qv[m], kb[m], 0.f);
+      }
+      transpose_reduce<LPR>(part, lane);
+      const int k = k0 + r / MI;
+      if (k < kTileMaxW) sbuf[my_pi][k] = sidx[my_pi][k] >= 0 ? part[0] * p.scale_log2 : -INFINITY;
+    }
+  }
+  __syncthreads();
+
+  // ---- softmax: thread t takes pair t / 2, slots [(t & 1) * 32, +32) ------
+  {
+    const int pi = threadIdx.x >> 1;
+    const int kbeg = (threadIdx.x & 1) * HALF;
+    float v[HALF];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < HALF; ++i) {
+      v[i] = kbeg + i < w ? sbuf[pi][kbeg + i] : -INFINITY;
+      mx = fmaxf(mx, v[i]);
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = mx == -INFINITY ? 0.f : mx;
+    __syncthreads();   // every score is in registers before the weights overwrite them
+    float l = 0.f;
+#pragma unroll
+    for (int i = 0; i < HALF; ++i) {
+      const Sc e = M::scalar(exp2f(v[i] - mx));
+      sp[pi][kbeg + i] = e;
+      l += M::to_float(e);
+    }
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    if ((threadIdx.x & 1) == 0) {
+      sl[pi] = l;
+      const int j = j0 + pi / G;
+      const int h = hkv * G + pi % G;
+      if (j < p.n_rows) p.lse[((int64_t)b * p.Hq + h) * p.n_rows + j] = mx + log2f(l);
+    }
+  }
+  __syncthreads();
+
+  // ---- O = P V: lane keeps the EPL output dims r*EPL.. of its MI pairs ----
+  float acc[MI][EPL];
+#pragma unroll
+  for (int m = 0; m < MI; ++m)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[m][e] = 0.f;
+  for (int k = 0; k < w; ++k) {
+    uint4 vb[MI];
+#pragma unroll
+    for (int m = 0; m < MI; ++m) {
+      const int row = sidx[pw0 + m * RPW + g][k];
+      vb[m] = row >= 0 ? ldg16(Vb + (int64_t)row * p.svs) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int m = 0; m < MI; ++m) M::axpy(sp[pw0 + m * RPW + g][k], vb[m], acc[m]);
+  }
+#pragma unroll
+  for (int m = 0; m < MI; ++m) {
+    const int pi = pw0 + m * RPW + g;
+    const int j = j0 + pi / G;
+    const int h = hkv * G + pi % G;
+    if (j < p.n_rows) {
+      const float lm = sl[pi];
+      const float inv = lm > 0.f ? 1.f / lm : 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[m][e] *= inv;
+      T* orow = reinterpret_cast<T*>(p.o) + b * p.sob + h * p.soh + (int64_t)j * p.sos + r * EPL;
+      stg16(orow, V::from_float(acc[m]));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Backward, query side: dQ and the (p, dS*scale) workspace.
 // Same grid and pair order as the forward.
 // ---------------------------------------------------------------------------

@@ -291,3 +291,25 @@ def test_window_tensor_core_path(esa, dtype, G, w, L, q_len):
     lse_ref = naive.lse_rows(q, k, torch.from_numpy(idx).to(DEV), torch.from_numpy(mask).to(DEV),
                              D ** -0.5, G)
     assert (lse_tc.double() / 1.4426950408889634 - lse_ref).abs().max().item() < 1e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("G,w,D,L,layer", [(1, 64, 128, 700, 5), (2, 33, 64, 515, 3), (4, 64, 128, 1000, 7),
+                                           (8, 7, 128, 300, 2), (32, 64, 64, 260, 6), (4, 50, 128, 4099, 1)])
+def test_tile_forward_matches_gather_forward(esa, dtype, G, w, D, L, layer):
+    """The slot-major tile forward (16-bit data, w <= 64) against the per-pair
+    gather forward and the fp32 oracle, including odd w and ragged tiles."""
+    g = torch.Generator().manual_seed(G * 31 + w + D)
+    Hkv = 2
+    Hq = Hkv * G
+    q = randn(1, Hq, L, D, dtype=dtype, gen=g)
+    k, v = randn(1, Hkv, L, D, dtype=dtype, gen=g), randn(1, Hkv, L, D, dtype=dtype, gen=g)
+    spec = esa.PatternSpec(layer, 8, w)
+    o_t, lse_t = esa.ops.forward(q, k, v, spec, D ** -0.5)
+    o_g, lse_g = esa.ops.forward(q, k, v, spec, D ** -0.5, gather_only=True)
+    assert (lse_t - lse_g).abs().max().item() < 1e-3
+    assert (o_t.float() - o_g.float()).abs().max().item() < 2e-2
+    idx, mask, _ = pattern.prepared_indices(Hq, w, layer, 8, L, L, L)
+    ro, _ = naive.naive_forward(q.float(), k.float(), v.float(), torch.from_numpy(idx).to(DEV),
+                                torch.from_numpy(mask).to(DEV), D ** -0.5, G, chunk=1024)
+    assert_close(o_t, ro, dtype, f"tile G{G} w{w} D{D} L{L}")
