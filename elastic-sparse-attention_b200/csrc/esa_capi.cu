@@ -248,7 +248,21 @@ int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
 
 template <typename T, int D>
 int launch_backward(const esa::AttnParams& p, cudaStream_t s) {
-  if (p.n_rows > 0) {
+  bool query_done = false;
+  if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
+    if (p.n_rows > 0 && p.pat.w <= esa::kTileMaxW && p.G <= esa::kTilePairs &&
+        esa::kTilePairs % p.G == 0 && !p.rows && p.n_rows >= 256 &&
+        !(p.flags & ESA_FLAG_GATHER_ONLY)) {
+      const int tq = esa::kTilePairs / p.G;
+      dim3 grid((p.n_rows + tq - 1) / tq, p.Hkv, p.B);
+      auto kern = esa::bwd_query_tile_kernel<T, D>;
+      if (int rc = prepare_smem(kern, esa::kTileBwdSmemBytes)) return rc;
+      kern<<<grid, 256, esa::kTileBwdSmemBytes, s>>>(p);
+      if (int rc = check_launch("backward (query side, tile)")) return rc;
+      query_done = true;
+    }
+  }
+  if (p.n_rows > 0 && !query_done) {
     const int rpc = rows_per_cta(p.G);
     const int wpad = (p.pat.w + 31) & ~31;
     const size_t smem = (size_t)kFwdWarps * 3 * wpad * sizeof(int);

@@ -179,7 +179,11 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
 // ---------------------------------------------------------------------------
 constexpr int kTilePairs = 128;
 constexpr int kTileMaxW = 64;
-constexpr int kTileSidxBytes = kTilePairs * kTileMaxW * 4;
+// Row strides of the per-pair shared arrays are odd in 32-bit words (65, and
+// 66 halves = 33 words) so that the pairs a warp touches fall in different banks.
+constexpr int kTileIdxStride = kTileMaxW + 1;
+constexpr int kTileSpStride = kTileMaxW + 2;
+constexpr int kTileSidxBytes = kTilePairs * kTileIdxStride * 4;
 constexpr int kTileSmemBytes = 2 * kTileSidxBytes + kTilePairs * 4;
 
 template <typename T, int D>
@@ -195,11 +199,12 @@ fwd_tile_kernel(const AttnParams p) {
   static_assert(MI * 2 == LPR, "two slots per transpose-reduce");
   constexpr int HALF = kTileMaxW / 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  int(*sidx)[kTileMaxW] = reinterpret_cast<int(*)[kTileMaxW]>(smem_raw);
+  int(*sidx)[kTileIdxStride] = reinterpret_cast<int(*)[kTileIdxStride]>(smem_raw);
   // fp32 scores; after the softmax the same bytes hold the weights in the
-  // input type, laid out as Sc[kTilePairs][kTileMaxW]
-  float(*sbuf)[kTileMaxW] = reinterpret_cast<float(*)[kTileMaxW]>(smem_raw + kTileSidxBytes);
-  Sc(*sp)[kTileMaxW] = reinterpret_cast<Sc(*)[kTileMaxW]>(&sbuf[0][0]);
+  // input type, laid out as Sc[kTilePairs][kTileSpStride]
+  float(*sbuf)[kTileIdxStride] =
+      reinterpret_cast<float(*)[kTileIdxStride]>(smem_raw + kTileSidxBytes);
+  Sc(*sp)[kTileSpStride] = reinterpret_cast<Sc(*)[kTileSpStride]>(&sbuf[0][0]);
   float* sl = reinterpret_cast<float*>(smem_raw + 2 * kTileSidxBytes);
   const int w = p.pat.w;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -343,6 +348,178 @@ fwd_tile_kernel(const AttnParams p) {
 }
 
 // ---------------------------------------------------------------------------
+// Backward, query side, slot-major tile variant (same tiling as
+// fwd_tile_kernel): pass 1a scores -> p = exp2(s - lse) (fp32, shared), pass
+// 1b dp = dO.v -> dS = p (dp - rowsum(dO O)), written to the (p, dS*scale)
+// workspace and kept in the input type in shared memory, pass 2 dQ = sum dS k.
+// Every pass walks the slots with all warps together, so the K / V rows the
+// tile's pairs share come from L1.
+// ---------------------------------------------------------------------------
+constexpr int kTileBwdSmemBytes = 2 * kTileSidxBytes + kTilePairs * kTileSpStride * 2;   // 16-bit dS
+
+template <typename T, int D>
+__global__ void __launch_bounds__(256, 2)
+bwd_query_tile_kernel(const AttnParams p) {
+  using L = Layout<T, D>;
+  using V = Vec<T>;
+  using M = Mix<T>;
+  using Sc = typename M::Scalar;
+  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  constexpr int PPW = kTilePairs / 8;
+  constexpr int MI = PPW / RPW;
+  static_assert(MI * 2 == LPR, "two slots per transpose-reduce");
+  constexpr int HALF = kTileMaxW / 2;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int(*sidx)[kTileIdxStride] = reinterpret_cast<int(*)[kTileIdxStride]>(smem_raw);
+  float(*sprob)[kTileIdxStride] =
+      reinterpret_cast<float(*)[kTileIdxStride]>(smem_raw + kTileSidxBytes);
+  Sc(*sds)[kTileSpStride] = reinterpret_cast<Sc(*)[kTileSpStride]>(smem_raw + 2 * kTileSidxBytes);
+  const int w = p.pat.w;
+  const int n = p.n_rows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane / LPR, r = lane % LPR;
+  const int G = p.G;
+  const int TQ = kTilePairs / G;
+  const int hkv = blockIdx.y, b = blockIdx.z;
+  const int j0 = blockIdx.x * TQ;
+
+  {
+    const int pi = threadIdx.x >> 1;
+    const int j = j0 + pi / G;
+    const int h = hkv * G + pi % G;
+    const int kbeg = (threadIdx.x & 1) * HALF;
+    if (j < n) {
+      const int pos = query_pos(p, j);
+      const RowWin rw = row_window(p.pat, pos);
+      const float t = head_weight(p.pat, h);
+      const float omt = __fsub_rn(1.f, t);
+      for (int k = kbeg; k < kbeg + HALF; ++k) {
+        int row = -1;
+        if (k < w) {
+          const int raw = raw_index(rw, k, t, omt);
+          if (raw <= pos) {
+            row = min(raw, p.kv_len - 1) - p.kv_offset;
+            if (row < 0 || row >= p.kv_rows) {
+              if (p.err) atomicOr(p.err, kErrKvRange);
+              row = -1;
+            }
+          }
+        }
+        sidx[pi][k] = row;
+      }
+    } else {
+      for (int k = kbeg; k < kbeg + HALF; ++k) sidx[pi][k] = -1;
+    }
+  }
+  __syncthreads();
+
+  const int pw0 = warp * PPW;
+  const int my_pi = pw0 + (r % MI) * RPW + g;   // pair whose totals this lane ends with
+  const int my_j = j0 + my_pi / G;
+  const int my_h = hkv * G + my_pi % G;
+  const bool my_live = my_j < n;
+  const T* Kb = reinterpret_cast<const T*>(p.k) + b * p.skb + hkv * p.skh + r * EPL;
+  const T* Vb = reinterpret_cast<const T*>(p.v) + b * p.svb + hkv * p.svh + r * EPL;
+  auto row_of = [&](const void* base, int64_t sb, int64_t sh, int64_t ss, int m) -> uint4 {
+    const int pi = pw0 + m * RPW + g;
+    const int j = j0 + pi / G;
+    const int h = hkv * G + pi % G;
+    return j < n ? ldg16_stream(reinterpret_cast<const T*>(base) + b * sb + h * sh +
+                                (int64_t)j * ss + r * EPL)
+                 : make_uint4(0, 0, 0, 0);
+  };
+
+  // ---- pass 1a: p = exp2(s * scale_log2 - lse) ----------------------------
+  {
+    const float lse2 = my_live ? p.lse[((int64_t)b * p.Hq + my_h) * n + my_j] : 0.f;
+    uint4 qv[MI];
+#pragma unroll
+    for (int m = 0; m < MI; ++m) qv[m] = row_of(p.q, p.sqb, p.sqh, p.sqs, m);
+    for (int k0 = 0; k0 < w; k0 += 2) {
+      float part[LPR];
+#pragma unroll
+      for (int s2 = 0; s2 < 2; ++s2) {
+        uint4 kb[MI];
+#pragma unroll
+        for (int m = 0; m < MI; ++m) {
+          const int row = sidx[pw0 + m * RPW + g][k0 + s2];
+          kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(qv[m], kb[m], 0.f);
+      }
+      transpose_reduce<LPR>(part, lane);
+      const int k = k0 + r / MI;
+      sprob[my_pi][k] = sidx[my_pi][k] >= 0 ? exp2f(part[0] * p.scale_log2 - lse2) : 0.f;
+    }
+  }
+
+  // ---- pass 1b: dp, dS, workspace ------------------------------------------
+  {
+    uint4 dv[MI];
+    float delta[MI];
+#pragma unroll
+    for (int m = 0; m < MI; ++m) {
+      dv[m] = row_of(p.dout, p.sdob, p.sdoh, p.sdos, m);
+      delta[m] = group_allreduce_sum<LPR>(M::dot(dv[m], row_of(p.o, p.sob, p.soh, p.sos, m), 0.f));
+    }
+    // delta of the pair this lane ends with: pair pw0 + (r % MI) * RPW + g
+    float my_delta = 0.f;
+#pragma unroll
+    for (int m = 0; m < MI; ++m) my_delta = (r % MI) == m ? delta[m] : my_delta;
+    float2* pds_pair = p.pds + ((int64_t)(b * p.Hq + my_h) * w) * n + my_j;
+    for (int k0 = 0; k0 < w; k0 += 2) {
+      float part[LPR];
+#pragma unroll
+      for (int s2 = 0; s2 < 2; ++s2) {
+        uint4 vb[MI];
+#pragma unroll
+        for (int m = 0; m < MI; ++m) {
+          const int row = sidx[pw0 + m * RPW + g][k0 + s2];
+          vb[m] = row >= 0 ? ldg16(Vb + (int64_t)row * p.svs) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(dv[m], vb[m], 0.f);
+      }
+      transpose_reduce<LPR>(part, lane);
+      const int k = k0 + r / MI;
+      const float pk = sprob[my_pi][k];
+      const float dsk = pk * (part[0] - my_delta) * p.scale;   // 0 for masked slots
+      if (my_live && k < w) pds_pair[(int64_t)k * n] = make_float2(pk, dsk);
+      sds[my_pi][k] = M::scalar(dsk);
+    }
+  }
+  __syncthreads();
+
+  // ---- pass 2: dQ = sum dS k ------------------------------------------------
+  float acc[MI][EPL];
+#pragma unroll
+  for (int m = 0; m < MI; ++m)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[m][e] = 0.f;
+  for (int k = 0; k < w; ++k) {
+    uint4 kb[MI];
+#pragma unroll
+    for (int m = 0; m < MI; ++m) {
+      const int row = sidx[pw0 + m * RPW + g][k];
+      kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int m = 0; m < MI; ++m) M::axpy(sds[pw0 + m * RPW + g][k], kb[m], acc[m]);
+  }
+#pragma unroll
+  for (int m = 0; m < MI; ++m) {
+    const int pi = pw0 + m * RPW + g;
+    const int j = j0 + pi / G;
+    const int h = hkv * G + pi % G;
+    if (j < n) {
+      T* dqrow = reinterpret_cast<T*>(p.dq) + b * p.sdqb + h * p.sdqh + (int64_t)j * p.sdqs + r * EPL;
+      stg16(dqrow, V::from_float(acc[m]));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Backward, query side: dQ and the (p, dS*scale) workspace.
 // Same grid and pair order as the forward.
 // ---------------------------------------------------------------------------
@@ -465,7 +642,7 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
 template <typename T, int D>
 struct KeyStage {
   static constexpr int kRowBytes = D * (int)sizeof(T);
-  static constexpr int kUsers = (4096 / kRowBytes) < 32 ? (4096 / kRowBytes) : 32;  // per stage
+  static constexpr int kUsers = (2048 / kRowBytes) < 32 ? (2048 / kRowBytes) : 32;  // per stage
   static constexpr int kStageBytes = kUsers * 2 * kRowBytes;                       // q + dO rows
   static constexpr int kWarpBytes = 2 * kStageBytes;
 };
@@ -485,7 +662,7 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 template <typename T, int D, int NW, int RW>
-__global__ void __launch_bounds__(NW * 32, 1)
+__global__ void __launch_bounds__(NW * 32, 3)
 bwd_key_kernel(const AttnParams p) {
   using L = Layout<T, D>;
   using V = Vec<T>;

@@ -313,3 +313,20 @@ def test_tile_forward_matches_gather_forward(esa, dtype, G, w, D, L, layer):
     ro, _ = naive.naive_forward(q.float(), k.float(), v.float(), torch.from_numpy(idx).to(DEV),
                                 torch.from_numpy(mask).to(DEV), D ** -0.5, G, chunk=1024)
     assert_close(o_t, ro, dtype, f"tile G{G} w{w} D{D} L{L}")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("G,w,D,L,layer", [(1, 64, 128, 700, 5), (2, 33, 64, 515, 3),
+                                           (4, 64, 128, 1000, 7), (8, 7, 128, 300, 2)])
+def test_tile_backward_against_oracle(esa, dtype, G, w, D, L, layer):
+    """Query-side tile backward (16-bit data, w <= 64, >= 256 rows) through the
+    module: all three gradients against the fp32 oracle."""
+    g = torch.Generator().manual_seed(G * 17 + w + D)
+    Hkv = 2
+    Hq = Hkv * G
+    q, do = randn(1, Hq, L, D, dtype=dtype, gen=g), randn(1, Hq, L, D, dtype=dtype, gen=g)
+    k, v = randn(1, Hkv, L, D, dtype=dtype, gen=g), randn(1, Hkv, L, D, dtype=dtype, gen=g)
+    o, dq, dk, dv = run_module(esa, q, k, v, do, layer, 8, w)
+    ref = run_oracle(q, k, v, do, layer, 8, w)
+    for got, want, t in zip((o, dq, dk, dv), ref, ("out", "dq", "dk", "dv")):
+        assert_close(got, want, dtype, f"tile bwd G{G} w{w} D{D} {t}")
