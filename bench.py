@@ -404,6 +404,69 @@ def bench_reference(args, world, rank):
                     "d2h_bytes_per_step": 0}}
 
 
+def bench_c5(args, world, rank, local):
+    """C5: B=1, 16 heads, D=128, L=2^20, bf16, the 8 P8 layers fwd+bwd, query
+    rows (and K/V rows) split across the ranks; each rank fetches the remote
+    K/V range its queries read over NCCL and returns partial dK/dV (strong
+    scaling: the total work is fixed)."""
+    import elastic_sparse_attention_b200 as esa
+    L5, H5 = 1 << 20, 16
+    if world == 1 and not torch.distributed.is_initialized():
+        import datetime
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        torch.distributed.init_process_group("nccl", rank=0, world_size=1,
+                                             timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    S = L5 // world
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    q = torch.randn(B, S, H5, D, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, S, H5, D, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, S, H5, D, device=dev, generator=g).to(torch.bfloat16)
+    do = torch.randn(B, S, H5 * D, device=dev, generator=g).to(torch.bfloat16)
+    mods = [esa.SequenceShardedElasticSparseAttention(layer, NL, H5, D, W, L5) for layer in range(NL)]
+    fetched = 0
+    for m in mods:
+        plan = m.plan(S, dev)
+        fetched = max(fetched, sum(b - a for (_, a, b) in plan.pieces_needed(rank)))
+
+    def step():
+        qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+        for m in mods:
+            out = m(qq, kk, vv)
+            out.backward(do)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    s_ = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record(s_)
+        for _ in range(args.steps):
+            step()
+        e1.record(s_)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    pairs = H5 * L5 * W - H5 * (W - 1) * W // 2 * 1   # rows < w-1 lose (w-1-i) slots at layer 0 only
+    useful = 14 * D * H5 * L5 * W * NL / (ms * 1e-3) / 1e12
+    return {"metric": "useful TFLOP/s, fwd+bwd, 1M ctx, sequence-sharded (C5)",
+            "value": round(useful, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1), seeded",
+            "config": {"workload": "C5: fwd+bwd of the 8 P8 layers, B=1, 16 heads, L=2^20, D=128, "
+                                   "query rows split over the ranks, remote K/V fetched with NCCL",
+                       "seq_len": L5, "rows_per_rank": S, "parallelism": f"sequence split x{world}",
+                       "max_rows_fetched_per_layer_per_rank": fetched},
+            "clocks": clocks.summary()}
+
+
 def profile_case(args):
     """One forward + backward of one layer at a reduced C3 shape (for ncu)."""
     import elastic_sparse_attention_b200 as esa
@@ -425,6 +488,8 @@ def profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", choices=["c3", "c5"], default="c3",
+                    help="c5: the 1M-token sequence-sharded configuration")
     ap.add_argument("--case", choices=["step", "one-layer"], default="step",
                     help="one-layer: a single fwd+bwd at --seq-len/--layer, for profilers")
     ap.add_argument("--seq-len", type=int, default=32768)
@@ -447,6 +512,13 @@ def main():
             print(json.dumps(line), flush=True)
         return
     world, rank, local = dist_init()
+    if args.workload == "c5":
+        line = bench_c5(args, world, rank, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+        return
     line = bench_ours(args, world, rank, local)
     if rank == 0:
         eff_per_step = line["value"] * line["ms_per_step"] * 1e-3 * 1e12

@@ -8,7 +8,8 @@ directory).
 from . import _lib, ops
 from .attention import ElasticSparseAttention, ElasticSparseAttentionFunction
 from .ops import PatternSpec
+from .sharded import SequenceShardedElasticSparseAttention
 
-__all__ = ["ElasticSparseAttention", "ElasticSparseAttentionFunction", "PatternSpec", "ops",
-           "_lib"]
+__all__ = ["ElasticSparseAttention", "ElasticSparseAttentionFunction", "PatternSpec",
+           "SequenceShardedElasticSparseAttention", "ops", "_lib"]
 __version__ = "0.1.0"

@@ -1,0 +1,79 @@
+"""GPU, 2 processes x 1 GPU each (NCCL): the sequence-sharded module against
+the fp32 oracle, outputs and all gradients.  Skipped when fewer than two GPUs
+are visible (the driver's single-GPU test run)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, cases, q_out):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    import elastic_sparse_attention_b200 as esa
+    from oracle import naive, pattern
+    errs = []
+    for (layer, S, Hq, Hkv, D, w, dtype) in cases:
+        L = S * world
+        g = torch.Generator().manual_seed(layer + 11)
+        q, k, v, do = (torch.randn(1, L, h, D, generator=g).to(dev, dtype) for h in (Hq, Hkv, Hkv, Hq))
+        sl = slice(rank * S, (rank + 1) * S)
+        qs, ks, vs = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
+        m = esa.SequenceShardedElasticSparseAttention(layer, 8, Hq, D, w, L, num_key_value_heads=Hkv)
+        out = m(qs, ks, vs)
+        out.backward(do[:, sl].reshape(1, S, Hq * D))
+        got = []
+        for t in (out.detach(), qs.grad, ks.grad, vs.grad):
+            lst = [torch.zeros_like(t) for _ in range(world)]
+            dist.all_gather(lst, t.contiguous())
+            got.append(torch.cat(lst, dim=1).float())
+        if rank == 0:
+            idx, mask, _ = pattern.prepared_indices(Hq, w, layer, 8, L, L, L)
+            ro, rdq, rdk, rdv = naive.naive_forward_backward_manual(
+                q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), do.transpose(1, 2),
+                torch.from_numpy(idx).to(dev), torch.from_numpy(mask).to(dev), D ** -0.5, Hq // Hkv)
+            want = [ro.transpose(1, 2).reshape(1, L, Hq * D), rdq.transpose(1, 2),
+                    rdk.transpose(1, 2), rdv.transpose(1, 2)]
+            for a, b in zip(got, want):
+                e = (a - b).abs()
+                tol = 2e-2 + 2.0 ** -8 * b.abs()
+                errs.append((float((e - tol).max()), float(e.mean())))
+    if rank == 0:
+        q_out.put(errs)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sequence_sharded_two_gpus():
+    cases = [(7, 1024, 8, 2, 128, 64, torch.bfloat16), (3, 768, 4, 4, 128, 64, torch.bfloat16),
+             (0, 1024, 8, 2, 128, 64, torch.bfloat16), (5, 512, 4, 2, 64, 64, torch.float16)]
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, cases, q_out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    errs = q_out.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for excess, mean in errs:
+        assert excess <= 0 and mean <= 2e-3, errs

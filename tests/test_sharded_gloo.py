@@ -1,0 +1,112 @@
+"""CPU, multi-process (gloo): the sequence-sharded module's exchange plan, KV
+fetch, reverse dK/dV exchange and fp32 reduction, with the kernels replaced
+by the oracle (the CUDA kernels are checked on their own by the GPU tests).
+Each rank runs on its shard; rank 0 compares the gathered output and
+gradients with one unsharded oracle run."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import naive, pattern
+
+
+class OracleOps:
+    """The subset of the kernel ops the sharded module calls, computed by the
+    fp32 oracle on the CPU (test infrastructure only)."""
+
+    @staticmethod
+    def pattern_indices(num_heads, spec, n_rows, device, rows=None, row_offset=0, clamp_len=0):
+        pos = rows.cpu().numpy() if rows is not None else np.arange(row_offset, row_offset + n_rows)
+        idx, mask = pattern.elastic_indices(pos, num_heads, spec.attention_length, spec.layer_idx,
+                                            spec.num_hidden_layers)
+        return torch.from_numpy(idx).to(device), torch.from_numpy(mask).to(device)
+
+    @staticmethod
+    def _local(q, k, spec, row_offset, kv_len, kv_offset):
+        Hq, n = q.shape[1], q.shape[2]
+        pos = np.arange(row_offset, row_offset + n)
+        idx, mask = pattern.elastic_indices(pos, Hq, spec.attention_length, spec.layer_idx,
+                                            spec.num_hidden_layers)
+        idx = np.clip(idx, 0, kv_len - 1) - kv_offset
+        assert (idx[mask.astype(bool)] >= 0).all() and (idx < k.shape[2]).all()
+        return torch.from_numpy(np.clip(idx, 0, None)), torch.from_numpy(mask)
+
+    @classmethod
+    def forward(cls, q, k, v, spec, scale, rows=None, row_offset=0, kv_len=None, kv_offset=0):
+        idx, mask = cls._local(q, k, spec, row_offset, kv_len, kv_offset)
+        do = torch.zeros_like(q)
+        out, *_ = naive.naive_forward_backward_manual(q, k, v, do, idx, mask, scale,
+                                                      q.shape[1] // k.shape[1])
+        return out.to(q.dtype), torch.zeros(q.shape[:3])
+
+    @classmethod
+    def backward(cls, q, k, v, o, lse, dout, spec, scale, rows=None, row_offset=0, kv_len=None,
+                 kv_offset=0):
+        idx, mask = cls._local(q, k, spec, row_offset, kv_len, kv_offset)
+        _, dq, dk, dv = naive.naive_forward_backward_manual(q, k, v, dout, idx, mask, scale,
+                                                            q.shape[1] // k.shape[1])
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
+
+
+def _worker(rank, world, port, layer, S, Hq, Hkv, D, w, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import elastic_sparse_attention_b200 as esa
+    L = S * world
+    g = torch.Generator().manual_seed(3)
+    q, k, v, do = (torch.randn(1, L, h, D, generator=g) for h in (Hq, Hkv, Hkv, Hq))
+    sl = slice(rank * S, (rank + 1) * S)
+    qs, ks, vs = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
+    m = esa.SequenceShardedElasticSparseAttention(layer, 8, Hq, D, w, L, num_key_value_heads=Hkv,
+                                                  ops=OracleOps)
+    out = m(qs, ks, vs)
+    out.backward(do[:, sl].reshape(1, S, Hq * D))
+    parts = [out.detach(), qs.grad, ks.grad, vs.grad]
+    gathered = []
+    for t in parts:
+        lst = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(lst, t.contiguous())
+        gathered.append(torch.cat(lst, dim=1))
+    if rank == 0:
+        idx, mask, _ = pattern.prepared_indices(Hq, w, layer, 8, L, L, L)
+        ro, rdq, rdk, rdv = naive.naive_forward_backward_manual(
+            q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), do.transpose(1, 2),
+            torch.from_numpy(idx), torch.from_numpy(mask), D ** -0.5, Hq // Hkv)
+        want = [ro.transpose(1, 2).reshape(1, L, Hq * D), rdq.transpose(1, 2),
+                rdk.transpose(1, 2), rdv.transpose(1, 2)]
+        errs = [float((a - b).abs().max()) for a, b in zip(gathered, want)]
+        result_q.put(errs)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+@pytest.mark.parametrize("world,layer,S,Hq,Hkv,D,w", [(2, 7, 96, 4, 2, 16, 16),
+                                                     (3, 4, 80, 2, 2, 16, 32),
+                                                     (2, 0, 70, 2, 1, 8, 16)])
+def test_sequence_sharded_matches_unsharded(world, layer, S, Hq, Hkv, D, w):
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, layer, S, Hq, Hkv, D, w, result_q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    errs = result_q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert max(errs) < 1e-4, errs
