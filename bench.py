@@ -426,10 +426,11 @@ def bench_c5(args, world, rank, local):
     v = torch.randn(B, S, H5, D, device=dev, generator=g).to(torch.bfloat16)
     do = torch.randn(B, S, H5 * D, device=dev, generator=g).to(torch.bfloat16)
     mods = [esa.SequenceShardedElasticSparseAttention(layer, NL, H5, D, W, L5) for layer in range(NL)]
-    fetched = 0
+    fetched = 0   # largest number of remote K/V rows any rank fetches for one layer
     for m in mods:
         plan = m.plan(S, dev)
-        fetched = max(fetched, sum(b - a for (_, a, b) in plan.pieces_needed(rank)))
+        fetched = max([fetched] + [sum(b - a for (_, a, b) in plan.pieces_needed(r))
+                                   for r in range(world)])
 
     def step():
         qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
@@ -453,7 +454,6 @@ def bench_c5(args, world, rank, local):
     t = torch.tensor([ms], device=dev)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = float(t.item())
-    pairs = H5 * L5 * W - H5 * (W - 1) * W // 2 * 1   # rows < w-1 lose (w-1-i) slots at layer 0 only
     useful = 14 * D * H5 * L5 * W * NL / (ms * 1e-3) / 1e12
     return {"metric": "useful TFLOP/s, fwd+bwd, 1M ctx, sequence-sharded (C5)",
             "value": round(useful, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
