@@ -38,7 +38,9 @@ class EsaProblem(ctypes.Structure):
                 ("q_len", ctypes.c_int64), ("kv_len", ctypes.c_int64),
                 ("kv_offset", ctypes.c_int64), ("kv_rows", ctypes.c_int64),
                 ("row_offset", ctypes.c_int64), ("rows", ctypes.c_void_p),
-                ("scale", ctypes.c_float), ("flags", ctypes.c_int32)]
+                ("scale", ctypes.c_float), ("flags", ctypes.c_int32),
+                ("dropout_p", ctypes.c_float), ("reserved", ctypes.c_int32),
+                ("dropout_seed", ctypes.c_uint64), ("weights", ctypes.c_void_p)]
 
 
 class EsaError(RuntimeError):
@@ -108,9 +110,12 @@ def stream_handle(device: torch.device) -> int:
 def problem(*, dtype: torch.dtype, batch: int, num_heads: int, num_kv_heads: int, head_dim: int,
             attn_length: int, layer_idx: int, num_hidden_layers: int, q_len: int, kv_len: int,
             kv_offset: int = 0, kv_rows: int | None = None, row_offset: int = 0,
-            rows: torch.Tensor | None = None, scale: float, flags: int = 0) -> EsaProblem:
+            rows: torch.Tensor | None = None, scale: float, flags: int = 0,
+            dropout_p: float = 0.0, dropout_seed: int = 0,
+            weights: torch.Tensor | None = None) -> EsaProblem:
     if dtype not in DTYPES:
         raise TypeError(f"unsupported dtype {dtype}; expected float32, bfloat16 or float16")
     return EsaProblem(DTYPES[dtype], batch, num_heads, num_kv_heads, head_dim, attn_length,
                       layer_idx, num_hidden_layers, q_len, kv_len, kv_offset,
-                      kv_len if kv_rows is None else kv_rows, row_offset, ptr(rows), scale, flags)
+                      kv_len if kv_rows is None else kv_rows, row_offset, ptr(rows), scale, flags,
+                      dropout_p, 0, dropout_seed, ptr(weights))

@@ -8,16 +8,22 @@ signature and the same ``(attn_output [B, q_len, H*D], attn_weights)`` result.
 Differences, all deliberate:
 
 * Every ``implementation`` value ("triton", "naive", "dense") is accepted and
-  validated as in the reference (:412-417) but runs the same CUDA path; there
-  is no Triton, no PyTorch fallback and no CPU path.  ``attn_weights`` is
-  ``None`` (as the reference's triton and dense paths return, :622, :726).
+  validated as in the reference (:412-417) and runs on the CUDA kernels; there
+  is no Triton, no PyTorch fallback and no CPU path.  As in the reference,
+  ``implementation="naive"`` returns the softmax weights ``[B, H, q_len, w]``
+  (:673-680, here not differentiable) and the others return ``None``
+  (:622, :726).
 * The pattern is computed inside the kernels from (position, head, slot), so
   nothing of size ``[H, max_seq_len, w]`` is built at construction (the
   reference builds it on the CPU, :454-468).  ``sparse_attention_indices``,
   ``sparse_causal_mask`` and ``full_attention_mask`` are still available, built
   lazily on the GPU on first access, bit-exact with the reference buffers.
-* ``attention_dropout`` is stored but not applied, like the reference's triton
-  path (which has no dropout); a one-time warning says so when it is > 0.
+* ``attention_dropout`` is applied where the reference applies it: in
+  training mode for the "naive" (:674) and "dense" (:721) implementations;
+  the "triton" implementation ignores it, as the reference's Triton kernel
+  does.  The keep mask comes from an in-kernel counter-based generator
+  (Philox4x32-10) seeded from torch's CPU generator, so it differs from
+  torch.dropout's mask but has the same distribution and scaling.
 """
 from __future__ import annotations
 
@@ -64,18 +70,25 @@ class ElasticSparseAttentionFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, k, v, pattern: PatternSpec, sm_scale: float, num_kv_groups: int,
-                rows: Optional[torch.Tensor] = None):
+                rows: Optional[torch.Tensor] = None, dropout_p: float = 0.0,
+                dropout_seed: int = 0, return_weights: bool = False):
         if q.shape[1] != k.shape[1] * num_kv_groups:
             raise ValueError("num_kv_groups does not match the query / key head counts")
         q, k, v = (ops.as_kernel_operand(t) for t in (q, k, v))
-        o, lse = ops.forward(q, k, v, pattern, sm_scale, rows=rows)
+        res = ops.forward(q, k, v, pattern, sm_scale, rows=rows, dropout_p=dropout_p,
+                          dropout_seed=dropout_seed, return_weights=return_weights)
+        o, lse = res[0], res[1]
         ctx.save_for_backward(q, k, v, o, lse, rows)
         ctx.pattern = pattern
         ctx.sm_scale = sm_scale
+        ctx.dropout = (dropout_p, dropout_seed)
+        if return_weights:
+            ctx.mark_non_differentiable(res[2])
+            return o, res[2]
         return o
 
     @staticmethod
-    def backward(ctx, do):
+    def backward(ctx, do, *unused):
         q, k, v, o, lse, rows = ctx.saved_tensors
         do = ops.as_kernel_operand(do)
         spec = ctx.pattern
@@ -87,8 +100,9 @@ class ElasticSparseAttentionFunction(torch.autograd.Function):
             seq = q.shape[2]
         _ensure_monotone(q.shape[1], spec, max(seq, 2), q.device)
         dq, dk, dv = ops.backward(q, k, v, o, lse, do, spec, ctx.sm_scale, rows=rows,
-                                  sorted_rows=sorted_rows, row_perm=perm)
-        return dq, dk, dv, None, None, None, None
+                                  sorted_rows=sorted_rows, row_perm=perm,
+                                  dropout_p=ctx.dropout[0], dropout_seed=ctx.dropout[1])
+        return dq, dk, dv, None, None, None, None, None, None, None
 
 
 class ElasticSparseAttention(nn.Module):
@@ -129,9 +143,9 @@ class ElasticSparseAttention(nn.Module):
         if max_seq_len > ops.MAX_POSITION:
             raise ValueError(f"max_seq_len ({max_seq_len}) above {ops.MAX_POSITION} is not "
                              "supported (float32 position arithmetic)")
-        if attention_dropout > 0:
-            logger.warning("attention_dropout=%s is not applied (as in the reference's triton "
-                           "path)", attention_dropout)
+        if attention_dropout > 0 and implementation == "triton":
+            logger.warning("attention_dropout=%s is not applied by implementation='triton' (as "
+                           "in the reference's Triton kernel)", attention_dropout)
         self.pattern = PatternSpec(layer_idx, num_hidden_layers, attention_length)
         self._buffers_cache: dict = {}
 
@@ -202,13 +216,18 @@ class ElasticSparseAttention(nn.Module):
                                       query_states.device)
         elif q_seq_len > kv_seq_len:
             raise ValueError(f"q_len ({q_seq_len}) > kv_len ({kv_seq_len}) needs cache_position")
-        attn_output = ElasticSparseAttentionFunction.apply(
+        dropout_p = (self.attention_dropout if self.training and
+                     self.implementation in ("naive", "dense") else 0.0)
+        seed = int(torch.randint(0, 2 ** 62, (1,)).item()) if dropout_p > 0 else 0
+        want_weights = self.implementation == "naive"
+        res = ElasticSparseAttentionFunction.apply(
             query_states, key_states, value_states, self.pattern, self.scaling,
-            self.num_kv_groups, rows)
+            self.num_kv_groups, rows, dropout_p, seed, want_weights)
+        attn_output, attn_weights = (res[0], res[1]) if want_weights else (res, None)
         batch_size, _, q_len, head_dim = query_states.shape
         hidden_dim = self.num_attention_heads * head_dim
         attn_output = attn_output.transpose(1, 2).reshape(batch_size, q_len, hidden_dim)
-        return attn_output, None
+        return attn_output, attn_weights
 
     @staticmethod
     def _prepare_rows(cache_position, q_seq_len: int, kv_seq_len: int, device) -> torch.Tensor:

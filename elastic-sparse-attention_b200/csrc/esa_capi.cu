@@ -96,6 +96,10 @@ int check_problem(const esa_problem_t* pb) {
   if (pb->row_offset < 0 || pb->row_offset + pb->q_len > kMaxPosition)
     return fail(ESA_ERR_INVALID, "row_offset out of range");
   if (!std::isfinite(pb->scale)) return fail(ESA_ERR_INVALID, "scale must be finite");
+  if (!(pb->dropout_p >= 0.f && pb->dropout_p <= 1.f))
+    return fail(ESA_ERR_INVALID, "dropout_p must be in [0, 1]");
+  if (pb->weights && reinterpret_cast<uintptr_t>(pb->weights) % 4)
+    return fail(ESA_ERR_INVALID, "weights must be 4-byte aligned");
   return ESA_OK;
 }
 
@@ -117,6 +121,13 @@ esa::AttnParams base_params(const esa_problem_t* pb) {
   p.scale_log2 = pb->scale * esa::kLog2e;
   p.alpha_zero = pb->layer_idx == 0;   // alpha = layer_idx / max(nl - 1, 1) == 0
   p.flags = pb->flags;
+  if (pb->dropout_p > 0.f) {
+    const double t = (double)pb->dropout_p * 4294967296.0;
+    p.drop_threshold = t >= 4294967295.0 ? 0xFFFFFFFFu : (uint32_t)t;
+    p.keep_scale = pb->dropout_p < 1.f ? 1.f / (1.f - pb->dropout_p) : 0.f;
+  }
+  p.seed = pb->dropout_seed;
+  p.weights = pb->weights;
   return p;
 }
 
@@ -141,6 +152,11 @@ int prepare_smem(K kernel, size_t bytes) {
       return fail(ESA_ERR_CUDA, "cannot reserve %zu bytes of shared memory", bytes);
   }
   return ESA_OK;
+}
+
+// Dropout and the weights output are implemented in the per-pair gather kernels.
+bool needs_gather(const esa::AttnParams& p) {
+  return p.drop_threshold || p.weights || (p.flags & ESA_FLAG_GATHER_ONLY);
 }
 
 // ---- tensor-core sliding-window path (alpha == 0) -------------------------
@@ -181,7 +197,7 @@ bool encode_map(CUtensorMap* m, const void* ptr, bool fp16, int64_t D, int64_t r
 template <typename T, int D>
 int window_heads(const esa::AttnParams& p, bool alpha_zero, int flags) {
   if (std::is_same<T, float>::value || D != esa::kWinHeadDim) return 0;
-  if (!alpha_zero || (flags & ESA_FLAG_GATHER_ONLY) || p.rows) return 0;
+  if (!alpha_zero || needs_gather(p) || p.rows) return 0;
   const int ht = (p.G % 4 == 0) ? 4 : (p.G == 2 ? 2 : 0);
   if (!ht) return 0;
   const int qt = esa::kWinRows / ht;
@@ -227,7 +243,7 @@ int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
   if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
     // slot-major tile kernel: 128 pairs per CTA share their K/V rows through L1
     if (p.pat.w <= esa::kTileMaxW && p.G <= esa::kTilePairs && esa::kTilePairs % p.G == 0 &&
-        !p.rows && p.n_rows >= 256 && !(p.flags & ESA_FLAG_GATHER_ONLY)) {
+        !p.rows && p.n_rows >= 256 && !needs_gather(p)) {
       const int tq = esa::kTilePairs / p.G;
       dim3 grid((p.n_rows + tq - 1) / tq, p.Hkv, p.B);
       auto kern = esa::fwd_tile_kernel<T, D>;
@@ -251,8 +267,7 @@ int launch_backward(const esa::AttnParams& p, cudaStream_t s) {
   bool query_done = false;
   if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
     if (p.n_rows > 0 && p.pat.w <= esa::kTileMaxW && p.G <= esa::kTilePairs &&
-        esa::kTilePairs % p.G == 0 && !p.rows && p.n_rows >= 256 &&
-        !(p.flags & ESA_FLAG_GATHER_ONLY)) {
+        esa::kTilePairs % p.G == 0 && !p.rows && p.n_rows >= 256 && !needs_gather(p)) {
       const int tq = esa::kTilePairs / p.G;
       dim3 grid((p.n_rows + tq - 1) / tq, p.Hkv, p.B);
       auto kern = esa::bwd_query_tile_kernel<T, D>;

@@ -245,6 +245,31 @@ __device__ __forceinline__ void axpy_f32(float s, const uint4& b, float* acc) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Counter-based random numbers for dropout: Philox4x32 with 10 rounds, as
+// published by Salmon, Moraes, Dror and Shaw ("Parallel random numbers: as
+// easy as 1, 2, 3", SC 2011): per round two 32x32->64 multiplications by the
+// paper's constants and a xor with the key; the key advances by the paper's
+// Weyl increments between rounds.  Pure function of (counter, key).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    if (i) { k.x += 0x9E3779B9u; k.y += 0xBB67AE85u; }
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+  }
+  return c;
+}
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
 __device__ __forceinline__ uint4 ldg16(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }

@@ -127,11 +127,19 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
     // values so that they add up to one exactly as used.
     float lsum = 0.f;
     for (int k = lane; k < wpad; k += 32) {
-      const Sc e = M::scalar(exp2f(ssc[k] - mx));
-      sps[k] = e;
+      Sc e = M::scalar(exp2f(ssc[k] - mx));
       lsum += M::to_float(e);
+      if (p.drop_threshold && k < w)   // dropout acts on the normalised weights (ref :674)
+        e = dropout_keep(p, pos, b * p.Hq + h, k) ? M::scalar(M::to_float(e) * p.keep_scale)
+                                                   : M::scalar(0.f);
+      sps[k] = e;
     }
     const float l = warp_sum(lsum);
+    if (p.weights) {   // the naive path's attn_weights (ref :673-674)
+      T* wrow = reinterpret_cast<T*>(p.weights) + (((int64_t)b * p.Hq + h) * p.n_rows + j) * w;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      for (int k = lane; k < w; k += 32) wrow[k] = from_f32<T>(M::to_float(sps[k]) * inv);
+    }
     __syncwarp();
 
     float acc[EPL];
@@ -596,7 +604,17 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
       float pk = 0.f, dsk = 0.f;
       if (sidx[k] >= 0) {
         pk = exp2f(ps[0] * p.scale_log2 - lse2);
-        dsk = pk * (pp[0] - delta) * p.scale;
+        float dpk = pp[0];
+        if (p.drop_threshold) {
+          // the same keep mask as the forward: dP = mask / (1 - p) * dO.v and
+          // the weight used for dV is the kept, rescaled one
+          const bool keep = dropout_keep(p, pos, b * p.Hq + h, k);
+          dpk = keep ? dpk * p.keep_scale : 0.f;
+          dsk = pk * (dpk - delta) * p.scale;
+          pk = keep ? pk * p.keep_scale : 0.f;
+        } else {
+          dsk = pk * (dpk - delta) * p.scale;
+        }
       }
       if (k < w) pds_row[(int64_t)k * n] = make_float2(pk, dsk);
       sds[k] = M::scalar(dsk);

@@ -39,7 +39,20 @@ struct AttnParams {
   int* err;                    // optional device error word (bit flags)
   bool alpha_zero;             // layer_idx == 0: the pattern is a causal window of w keys
   int flags;                   // ESA_FLAG_* of the call
+  // Dropout of the softmax weights: keep when the Philox word of
+  // (position, batch * Hq + head, slot / 4) under key `seed` is >= threshold.
+  uint32_t drop_threshold;     // 0 = no dropout
+  float keep_scale;            // 1 / (1 - dropout_p)
+  uint64_t seed;
+  void* weights;               // optional [B, Hq, n_rows, w] weights output (input dtype)
 };
+
+__device__ __forceinline__ bool dropout_keep(const AttnParams& p, int pos, int bh, int k) {
+  const uint4 r = philox4x32_10(make_uint4((uint32_t)pos, (uint32_t)bh, (uint32_t)(k >> 2), 0u),
+                                make_uint2((uint32_t)p.seed, (uint32_t)(p.seed >> 32)));
+  const uint32_t word = (k & 3) == 0 ? r.x : (k & 3) == 1 ? r.y : (k & 3) == 2 ? r.z : r.w;
+  return word >= p.drop_threshold;
+}
 
 enum ErrBits : int {
   kErrKvRange = 1,  // an index fell outside the k/v rows handed to the launch

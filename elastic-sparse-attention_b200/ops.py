@@ -76,46 +76,56 @@ def pattern_audit(num_heads: int, spec: PatternSpec, seq_len: int, device: torch
 
 
 def _problem(q, k, spec: PatternSpec, scale: float, rows, row_offset: int, kv_len: int,
-             kv_offset: int, flags: int = 0):
+             kv_offset: int, flags: int = 0, dropout_p: float = 0.0, dropout_seed: int = 0,
+             weights=None):
     B, Hq, Lq, D = q.shape
     return _lib.problem(dtype=q.dtype, batch=B, num_heads=Hq, num_kv_heads=k.shape[1], head_dim=D,
                         attn_length=spec.attention_length, layer_idx=spec.layer_idx,
                         num_hidden_layers=spec.num_hidden_layers, q_len=Lq, kv_len=kv_len,
                         kv_offset=kv_offset, kv_rows=k.shape[2], row_offset=row_offset,
-                        rows=rows, scale=scale, flags=flags)
+                        rows=rows, scale=scale, flags=flags, dropout_p=dropout_p,
+                        dropout_seed=dropout_seed, weights=weights)
 
 
 def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: PatternSpec, scale: float,
             rows: torch.Tensor | None = None, row_offset: int = 0, kv_len: int | None = None,
-            kv_offset: int = 0, out: torch.Tensor | None = None, gather_only: bool = False):
+            kv_offset: int = 0, out: torch.Tensor | None = None, gather_only: bool = False,
+            dropout_p: float = 0.0, dropout_seed: int = 0, return_weights: bool = False):
     """Forward pass.  Returns (o [B, Hq, Lq, D] as a view of a [B, Lq, Hq, D]
-    buffer, lse float32 [B, Hq, Lq] base 2).  ``gather_only`` keeps sliding-
-    window layers on the CUDA-core kernel (for cross-checking the two paths)."""
+    buffer, lse float32 [B, Hq, Lq] base 2) and, with ``return_weights``, the
+    softmax weights after dropout [B, Hq, Lq, w] in the input dtype.
+    ``gather_only`` keeps sliding-window layers on the CUDA-core kernel (for
+    cross-checking the two paths)."""
     dev = _check_device(q, k, v)
     B, Hq, Lq, D = q.shape
     if out is None:
         out = torch.empty((B, Lq, Hq, D), dtype=q.dtype, device=dev).transpose(1, 2)
     lse = torch.empty((B, Hq, Lq), dtype=torch.float32, device=dev)
+    weights = (torch.empty((B, Hq, Lq, spec.attention_length), dtype=q.dtype, device=dev)
+               if return_weights else None)
     pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
-                  kv_offset, _lib.FLAG_GATHER_ONLY if gather_only else 0)
+                  kv_offset, _lib.FLAG_GATHER_ONLY if gather_only else 0, dropout_p,
+                  dropout_seed, weights)
     lib = _lib.load()
     with torch.cuda.device(dev):
         _lib.check(lib.esa_forward(ctypes.byref(pb), _lib.tensor4(q), _lib.tensor4(k),
                                    _lib.tensor4(v), _lib.tensor4(out), lse.data_ptr(),
                                    _lib.stream_handle(dev)), "esa_forward")
-    return out, lse
+    return (out, lse, weights) if return_weights else (out, lse)
 
 
 def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
              rows: torch.Tensor | None = None, row_offset: int = 0, kv_len: int | None = None,
-             kv_offset: int = 0, sorted_rows=None, row_perm=None, workspace=None):
-    """Backward pass.  Returns (dq, dk, dv) in the input dtype."""
+             kv_offset: int = 0, sorted_rows=None, row_perm=None, workspace=None,
+             dropout_p: float = 0.0, dropout_seed: int = 0):
+    """Backward pass.  Returns (dq, dk, dv) in the input dtype.  With dropout,
+    pass the forward's dropout_p and dropout_seed (the keep mask is rebuilt)."""
     dev = _check_device(q, k, v, o, lse, dout)
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
     pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
-                  kv_offset)
+                  kv_offset, 0, dropout_p, dropout_seed)
     lib = _lib.load()
     need = lib.esa_backward_workspace_size(ctypes.byref(pb))
     if workspace is None or workspace.numel() < need:

@@ -62,6 +62,15 @@ typedef struct {
  *                         [kv_offset, kv_offset + kv_rows); for a plain call
  *                         kv_offset = 0 and kv_rows = kv_len
  *   scale              -- softmax scale, the reference uses head_dim ** -0.5
+ *   dropout_p          -- probability of dropping a softmax weight (the
+ *                         reference's naive/dense paths in training, :674,
+ *                         :721); 0 disables.  The keep mask is a function of
+ *                         (dropout_seed, batch, head, position, slot), so the
+ *                         backward reproduces it from the same problem.
+ *   weights            -- optional output of esa_forward: the softmax weights
+ *                         after dropout, input dtype, contiguous
+ *                         [B, num_heads, q_len, attn_length] (the reference's
+ *                         naive attn_weights, :673-680); NULL = not written
  */
 typedef struct {
   int32_t dtype;
@@ -80,6 +89,10 @@ typedef struct {
   const int64_t* rows;
   float scale;
   int32_t flags;   /* ESA_FLAG_* bits, 0 by default */
+  float dropout_p;
+  int32_t reserved;
+  uint64_t dropout_seed;
+  void* weights;
 } esa_problem_t;
 
 /* flags: run every layer on the CUDA-core gather kernels, also where the

@@ -165,3 +165,23 @@ def naive_forward_backward_manual(q, k, v, do, idx, mask, scale: float, num_kv_g
     dk = dkr.view(B, Hkv, num_kv_groups, Lkv, D).sum(2)
     dv = dvr.view(B, Hkv, num_kv_groups, Lkv, D).sum(2)
     return out, dq, dk, dv
+
+
+def naive_forward_backward_keep(q, k, v, do, idx, mask, scale: float, num_kv_groups: int,
+                                keep, p: float):
+    """Naive path with dropout given as an explicit keep mask [B, H, n, w]:
+    weights = softmax(scores) * keep / (1 - p) (``torch.dropout`` semantics,
+    ``:674``), out = weights . V, gradients by autograd.  float32 throughout.
+    Returns (out, weights, dq, dk, dv)."""
+    qf, kf, vf = (t.detach().float().clone().requires_grad_(True) for t in (q, k, v))
+    kk, vv = kf, vf
+    if num_kv_groups > 1:
+        kk = kf.repeat_interleave(num_kv_groups, dim=1)
+        vv = vf.repeat_interleave(num_kv_groups, dim=1)
+    gk, gv = _gather_rows(kk, idx), _gather_rows(vv, idx)
+    s = torch.einsum("bhcd,bhcwd->bhcw", qf, gk) * scale
+    s = s.masked_fill(mask.unsqueeze(0) < 1, torch.finfo(torch.float32).min)
+    w = torch.softmax(s, dim=-1) * keep.float() / (1.0 - p)
+    out = torch.einsum("bhcw,bhcwd->bhcd", w, gv)
+    dq, dk, dv = torch.autograd.grad(out, (qf, kf, vf), do.float())
+    return out.detach(), w.detach(), dq, dk, dv

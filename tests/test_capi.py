@@ -40,6 +40,8 @@ def test_struct_layout_matches_header(tmp_path, esa):
         " offsetof(esa_problem_t, q_len), offsetof(esa_problem_t, rows),"
         " offsetof(esa_problem_t, scale), sizeof(esa_tensor_t),"
         " offsetof(esa_tensor_t, stride_s), offsetof(esa_problem_t, row_offset));\n"
+        ' printf(" %zu %zu\\n", offsetof(esa_problem_t, dropout_seed),'
+        " offsetof(esa_problem_t, weights));\n"
         " return 0; }\n")
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-std=c99", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)],
@@ -48,7 +50,7 @@ def test_struct_layout_matches_header(tmp_path, esa):
                                           check=True).stdout.split()]
     P, T = esa._lib.EsaProblem, esa._lib.EsaTensor
     want = [ctypes.sizeof(P), P.q_len.offset, P.rows.offset, P.scale.offset, ctypes.sizeof(T),
-            T.stride_s.offset, P.row_offset.offset]
+            T.stride_s.offset, P.row_offset.offset, P.dropout_seed.offset, P.weights.offset]
     assert got == want
 
 
@@ -56,7 +58,8 @@ def _problem(esa, **kw):
     base = dict(dtype=esa._lib.DTYPES[__import__("torch").bfloat16], batch=1, num_heads=4,
                 num_kv_heads=2, head_dim=128, attn_length=64, layer_idx=3, num_hidden_layers=8,
                 q_len=16, kv_len=16, kv_offset=0, kv_rows=16, row_offset=0, rows=None,
-                scale=128 ** -0.5, flags=0)
+                scale=128 ** -0.5, flags=0, dropout_p=0.0, reserved=0, dropout_seed=0,
+                weights=None)
     base.update(kw)
     return esa._lib.EsaProblem(**base)
 

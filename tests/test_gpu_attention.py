@@ -330,3 +330,58 @@ def test_tile_backward_against_oracle(esa, dtype, G, w, D, L, layer):
     ref = run_oracle(q, k, v, do, layer, 8, w)
     for got, want, t in zip((o, dq, dk, dv), ref, ("out", "dq", "dk", "dv")):
         assert_close(got, want, dtype, f"tile bwd G{G} w{w} D{D} {t}")
+
+
+def test_naive_implementation_returns_reference_weights(esa, naive_small):
+    """implementation="naive" returns attn_weights like the reference's naive
+    path (:673-680); compared with the weights the reference itself produced."""
+    meta_all, arrays = naive_small
+    for meta in meta_all:
+        name, layer = meta["name"], meta["layer"]
+        dtype = torch.float32 if meta["dtype"] == "float32" else torch.bfloat16
+        q, k, v = (torch.from_numpy(arrays[f"{name}_{t}"]).to(DEV, dtype) for t in "qkv")
+        cp = meta["cache_position"]
+        m = esa.ElasticSparseAttention(layer, meta["nl"], meta["Hq"], meta["D"], meta["w"], meta["L"],
+                                       num_key_value_heads=meta["Hkv"], implementation="naive")
+        out, weights = m(q, k, v, cache_position=None if cp is None else torch.tensor(cp, device=DEV))
+        ref = torch.from_numpy(arrays[f"{name}_l{layer}_weights"]).to(DEV)
+        assert weights.shape == ref.shape and weights.dtype == dtype
+        tol = 1e-5 if dtype == torch.float32 else 1e-2
+        assert (weights.float() - ref).abs().max().item() <= tol, name
+        assert esa.ElasticSparseAttention(layer, meta["nl"], meta["Hq"], meta["D"], meta["w"],
+                                          meta["L"], num_key_value_heads=meta["Hkv"],
+                                          implementation="dense")(q, k, v, cache_position=None if cp is None else torch.tensor(cp, device=DEV))[1] is None
+
+
+@pytest.mark.parametrize("dtype,p", [(torch.float32, 0.3), (torch.bfloat16, 0.1)])
+def test_dropout_matches_oracle_with_same_mask(esa, dtype, p):
+    """Training-mode dropout of the naive implementation: the keep mask is
+    recovered from the returned weights, and outputs and gradients equal the
+    oracle run with that mask (so forward and backward use one mask)."""
+    g = torch.Generator().manual_seed(21)
+    B, Hq, Hkv, L, D, layer = 1, 4, 2, 400, 64, 5
+    q, do = randn(B, Hq, L, D, dtype=dtype, gen=g), randn(B, Hq, L, D, dtype=dtype, gen=g)
+    k, v = randn(B, Hkv, L, D, dtype=dtype, gen=g), randn(B, Hkv, L, D, dtype=dtype, gen=g)
+    m = esa.ElasticSparseAttention(layer, 8, Hq, D, 64, L, num_key_value_heads=Hkv,
+                                   attention_dropout=p, implementation="naive").train()
+    qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
+    out, weights = m(qq, kk, vv)
+    out.backward(do.transpose(1, 2).reshape(B, L, Hq * D))
+    idx, mask, _ = pattern.prepared_indices(Hq, 64, layer, 8, L, L, L)
+    ti, tm = torch.from_numpy(idx).to(DEV), torch.from_numpy(mask).to(DEV)
+    keep = (weights != 0) & (tm.unsqueeze(0) > 0)
+    frac = 1.0 - keep.float().sum().item() / tm.sum().item()
+    assert abs(frac - p) < 0.02, frac
+    ro, rw, rdq, rdk, rdv = naive.naive_forward_backward_keep(q, k, v, do, ti, tm, D ** -0.5,
+                                                              Hq // Hkv, keep, p)
+    o = out.detach().view(B, L, Hq, D).transpose(1, 2)
+    assert_close(weights, rw, dtype, "weights")
+    for got, want, t in ((o, ro, "out"), (qq.grad, rdq, "dq"), (kk.grad, rdk, "dk"),
+                         (vv.grad, rdv, "dv")):
+        assert_close(got, want, dtype, f"dropout {t}")
+    # eval mode and the triton implementation apply no dropout
+    m.eval()
+    o_eval, _ = m(q, k, v)
+    o_tri, w_tri = esa.ElasticSparseAttention(layer, 8, Hq, D, 64, L, num_key_value_heads=Hkv,
+                                              attention_dropout=p).train()(q, k, v)
+    assert w_tri is None and torch.allclose(o_eval.float(), o_tri.float(), atol=2e-2)
