@@ -346,7 +346,7 @@ def test_naive_implementation_returns_reference_weights(esa, naive_small):
         out, weights = m(q, k, v, cache_position=None if cp is None else torch.tensor(cp, device=DEV))
         ref = torch.from_numpy(arrays[f"{name}_l{layer}_weights"]).to(DEV)
         assert weights.shape == ref.shape and weights.dtype == dtype
-        tol = 1e-5 if dtype == torch.float32 else 1e-2
+        tol = 1e-5 if dtype == torch.float32 else 2e-2
         assert (weights.float() - ref).abs().max().item() <= tol, name
         assert esa.ElasticSparseAttention(layer, meta["nl"], meta["Hq"], meta["D"], meta["w"],
                                           meta["L"], num_key_value_heads=meta["Hkv"],
