@@ -467,6 +467,86 @@ def bench_c5(args, world, rank, local):
             "clocks": clocks.summary()}
 
 
+def bench_decode(args):
+    """Decode latency (one GPU): one new token (or --decode-rows tokens) per
+    sequence attends, through each of the 8 P8 layers, to its own K/V cache of
+    L=131072 rows (B=1, 32 query / 8 KV heads, D=128, bf16).  Timed per token
+    step with CUDA events around a CUDA-graph replay of the 8 layer forwards,
+    L2 flushed before every step (cold K/V rows); also the same with the
+    throughput gather kernel forced, and through the public module (eager
+    Python, and captured in a CUDA graph)."""
+    import elastic_sparse_attention_b200 as esa
+    dev = torch.device("cuda", 0)
+    n = args.decode_rows
+    g = torch.Generator(device=dev).manual_seed(3)
+    ks = [torch.randn(B, HKV, L, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(NL)]
+    vs = [torch.randn(B, HKV, L, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(NL)]
+    q = torch.randn(B, HQ, n, D, device=dev, generator=g).to(torch.bfloat16)
+    rows = torch.arange(L - n, L, device=dev)
+    specs = [esa.PatternSpec(layer, NL, W) for layer in range(NL)]
+    outs = [torch.empty(B, n, HQ, D, dtype=torch.bfloat16, device=dev).transpose(1, 2)
+            for _ in range(NL)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def layers(gather_only):
+        for layer in range(NL):
+            esa.ops.forward(q, ks[layer], vs[layer], specs[layer], D ** -0.5, rows=rows,
+                            out=outs[layer], gather_only=gather_only)
+
+    mods = [esa.ElasticSparseAttention(layer, NL, HQ, D, W, L, num_key_value_heads=HKV).eval()
+            for layer in range(NL)]
+
+    def module_step():
+        with torch.no_grad():
+            for layer in range(NL):
+                mods[layer](q, ks[layer], vs[layer], cache_position=rows)
+
+    def timed(fn, graph):
+        s_ = torch.cuda.current_stream()
+        if graph:
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                fn()
+            fn = gr.replay
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        times = []
+        for _ in range(max(args.steps, 20)):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s_)
+            fn()
+            e1.record(s_)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(times)
+
+    with ClockSampler(0) as clocks:
+        us = timed(lambda: layers(False), True)
+        us_gather = timed(lambda: layers(True), True)
+        us_module_graph = timed(module_step, True)
+        us_module = timed(module_step, False)
+    ref = esa.ops.forward(q, ks[NL - 1], vs[NL - 1], specs[NL - 1], D ** -0.5, rows=rows,
+                          gather_only=True)[0]
+    assert (outs[NL - 1].float() - ref.float()).abs().max().item() < 2e-2
+    kv_bytes = NL * HQ * n * W * 2 * D * 2
+    return {"metric": "decode latency, 8 P8 layers, 128k KV cache", "value": round(us, 2),
+            "unit": "us per token step", "n_gpus": 1, "steps": max(args.steps, 20),
+            "warmup": max(args.warmup, 3), "higher_is_better": False, "dtype": "bf16",
+            "data": "synthetic N(0,1), seeded",
+            "config": {"workload": f"decode: {n} new row(s) x 32q/8kv heads, D=128, w=64, "
+                                   "8 layers each with its own 131072-row K/V cache",
+                       "decode_rows": n, "kv_len": L, "l2": "256 MB written before every step",
+                       "timing": "median of per-step CUDA events around a CUDA graph replay"},
+            "gather_kernel_us": round(us_gather, 2),
+            "module_us": {"eager": round(us_module, 2), "cuda_graph": round(us_module_graph, 2)},
+            "kv_bytes_per_step": kv_bytes,
+            "clocks": clocks.summary()}
+
+
 def profile_case(args):
     """One forward + backward of one layer at a reduced C3 shape (for ncu)."""
     import elastic_sparse_attention_b200 as esa
@@ -488,8 +568,10 @@ def profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["c3", "c5"], default="c3",
-                    help="c5: the 1M-token sequence-sharded configuration")
+    ap.add_argument("--workload", choices=["c3", "c5", "decode"], default="c3",
+                    help="c5: the 1M-token sequence-sharded configuration; decode: "
+                         "per-token latency against a 128k K/V cache")
+    ap.add_argument("--decode-rows", type=int, default=1)
     ap.add_argument("--case", choices=["step", "one-layer"], default="step",
                     help="one-layer: a single fwd+bwd at --seq-len/--layer, for profilers")
     ap.add_argument("--seq-len", type=int, default=32768)
@@ -510,6 +592,9 @@ def main():
         line = bench_reference(args, world, rank)
         if line:
             print(json.dumps(line), flush=True)
+        return
+    if args.workload == "decode":
+        print(json.dumps(bench_decode(args)), flush=True)
         return
     world, rank, local = dist_init()
     if args.workload == "c5":

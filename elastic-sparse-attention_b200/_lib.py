@@ -21,8 +21,14 @@ FLAG_GATHER_ONLY = 1
 DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 # Every symbol exported by include/esa_b200.h.
-EXPORTED = ("esa_version", "esa_last_error", "esa_pattern", "esa_pattern_audit", "esa_forward",
-            "esa_backward_workspace_size", "esa_backward", "esa_backward_noalloc")
+EXPORTED = ("esa_version", "esa_last_error", "esa_device_errors", "esa_pattern",
+            "esa_pattern_audit", "esa_forward", "esa_backward_workspace_size", "esa_backward",
+            "esa_backward_noalloc")
+
+# ESA_DEVERR_* bits of the per-device error word
+DEVERR_KV_RANGE = 1
+DEVERR_TIMEOUT = 2
+DEVERR_QUERY_RANGE = 4
 
 
 class EsaTensor(ctypes.Structure):
@@ -69,6 +75,8 @@ def load() -> ctypes.CDLL:
         i32, i64 = ctypes.c_int32, ctypes.c_int64
         lib.esa_version.restype = ctypes.c_int
         lib.esa_last_error.restype = ctypes.c_char_p
+        lib.esa_device_errors.argtypes = [i32, ctypes.POINTER(i32), P]
+        lib.esa_device_errors.restype = ctypes.c_int
         lib.esa_pattern.argtypes = [i32, i32, i32, i32, i64, P, i64, i64, P, P, P]
         lib.esa_pattern.restype = ctypes.c_int
         lib.esa_pattern_audit.argtypes = [i32, i32, i32, i32, i64, P, P]

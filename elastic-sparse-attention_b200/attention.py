@@ -105,6 +105,19 @@ class ElasticSparseAttentionFunction(torch.autograd.Function):
         return dq, dk, dv, None, None, None, None, None, None, None
 
 
+def _forward_without_grad(q, k, v, pattern: PatternSpec, sm_scale: float, num_kv_groups: int,
+                          rows: Optional[torch.Tensor], dropout_p: float, dropout_seed: int,
+                          return_weights: bool):
+    """The forward of :class:`ElasticSparseAttentionFunction` for calls that
+    need no gradient (same results, no autograd bookkeeping)."""
+    if q.shape[1] != k.shape[1] * num_kv_groups:
+        raise ValueError("num_kv_groups does not match the query / key head counts")
+    q, k, v = (ops.as_kernel_operand(t) for t in (q, k, v))
+    res = ops.forward(q, k, v, pattern, sm_scale, rows=rows, dropout_p=dropout_p,
+                      dropout_seed=dropout_seed, return_weights=return_weights)
+    return (res[0], res[2]) if return_weights else res[0]
+
+
 class ElasticSparseAttention(nn.Module):
     """Elastic sparse attention with GQA; see the module docstring for the contract.
 
@@ -210,19 +223,27 @@ class ElasticSparseAttention(nn.Module):
             raise ValueError(
                 f"Input sequence length ({kv_seq_len}) exceeds the maximum length initialized "
                 f"in the module ({self.max_seq_len}).")
+        needs_grad = torch.is_grad_enabled() and (
+            query_states.requires_grad or key_states.requires_grad or value_states.requires_grad)
         rows = None
         if cache_position is not None:
             rows = self._prepare_rows(cache_position, q_seq_len, kv_seq_len,
-                                      query_states.device)
+                                      query_states.device, checked=needs_grad)
         elif q_seq_len > kv_seq_len:
             raise ValueError(f"q_len ({q_seq_len}) > kv_len ({kv_seq_len}) needs cache_position")
         dropout_p = (self.attention_dropout if self.training and
                      self.implementation in ("naive", "dense") else 0.0)
         seed = int(torch.randint(0, 2 ** 62, (1,)).item()) if dropout_p > 0 else 0
         want_weights = self.implementation == "naive"
-        res = ElasticSparseAttentionFunction.apply(
-            query_states, key_states, value_states, self.pattern, self.scaling,
-            self.num_kv_groups, rows, dropout_p, seed, want_weights)
+        if needs_grad:
+            res = ElasticSparseAttentionFunction.apply(
+                query_states, key_states, value_states, self.pattern, self.scaling,
+                self.num_kv_groups, rows, dropout_p, seed, want_weights)
+        else:
+            # inference: no autograd node, nothing saved
+            res = _forward_without_grad(query_states, key_states, value_states, self.pattern,
+                                        self.scaling, self.num_kv_groups, rows, dropout_p, seed,
+                                        want_weights)
         attn_output, attn_weights = (res[0], res[1]) if want_weights else (res, None)
         batch_size, _, q_len, head_dim = query_states.shape
         hidden_dim = self.num_attention_heads * head_dim
@@ -230,17 +251,37 @@ class ElasticSparseAttention(nn.Module):
         return attn_output, attn_weights
 
     @staticmethod
-    def _prepare_rows(cache_position, q_seq_len: int, kv_seq_len: int, device) -> torch.Tensor:
+    def _prepare_rows(cache_position, q_seq_len: int, kv_seq_len: int, device,
+                      checked: bool = True) -> torch.Tensor:
         """Query positions for ``cache_position`` as the reference indexes the
         ``[:kv_len]`` slice of its buffers (:607-608): negative entries wrap,
-        out-of-range entries raise IndexError."""
-        rows = torch.as_tensor(cache_position, device=device).to(torch.int64).reshape(-1)
+        out-of-range entries raise IndexError.
+
+        A host-side ``cache_position`` is checked on the host.  A device tensor
+        is checked with one device->host read when a backward will follow
+        (``checked``) and no CUDA graph is being captured.  Otherwise (decode
+        under ``no_grad``, graph capture) nothing waits for the GPU: the forward
+        kernel wraps negative entries itself, writes zeros for out-of-range
+        rows and records ``ESA_DEVERR_QUERY_RANGE``, read with
+        ``ops.device_errors()``."""
+        rows = torch.as_tensor(cache_position)
+        if rows.dtype != torch.int64:
+            rows = rows.to(torch.int64)
+        rows = rows.reshape(-1)
         if rows.numel() != q_seq_len:
             raise ValueError(f"cache_position has {rows.numel()} entries for q_len {q_seq_len}")
+        if not rows.is_cuda:
+            rows = torch.where(rows < 0, rows + kv_seq_len, rows)
+            if rows.numel() and (int(rows.min()) < 0 or int(rows.max()) >= kv_seq_len):
+                raise IndexError(f"cache_position out of range for kv_len {kv_seq_len}")
+            return rows.to(device).contiguous()
+        if not checked:
+            return rows.to(device).contiguous()
         rows = torch.where(rows < 0, rows + kv_seq_len, rows)
-        if rows.numel() and (int(rows.min()) < 0 or int(rows.max()) >= kv_seq_len):
+        if (rows.numel() and not torch.cuda.is_current_stream_capturing()
+                and bool(((rows < 0) | (rows >= kv_seq_len)).any())):
             raise IndexError(f"cache_position out of range for kv_len {kv_seq_len}")
-        return rows.contiguous()
+        return rows.to(device).contiguous()
 
     def extra_repr(self) -> str:
         return (f"layer_idx={self.layer_idx}, num_hidden_layers={self.num_hidden_layers}, "

@@ -7,6 +7,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <mutex>
 #include <cstdarg>
@@ -14,6 +15,7 @@
 #include <string>
 
 #include "esa_b200.h"
+#include "esa_decode.cuh"
 #include "esa_gather.cuh"
 #include "esa_pattern.cuh"
 #include "esa_window_tc.cuh"
@@ -144,6 +146,48 @@ constexpr int kKeyRowsPerWarp = 16;
 
 int rows_per_cta(int G) { return G >= 64 ? 1 : 64 / G; }
 
+// Per-device addresses of a __device__ variable of this library, looked up
+// once per device (cudaGetSymbolAddress with that device current) and cached.
+constexpr int kMaxDevices = 64;
+struct SymbolAddresses {
+  std::mutex mu;
+  void* addr[kMaxDevices] = {};
+};
+
+int symbol_address(const void* symbol, SymbolAddresses& cache, const char* what, void** out) {
+  int dev = -1;
+  const cudaError_t de = cudaGetDevice(&dev);
+  if (de != cudaSuccess) return fail(ESA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(de));
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(ESA_ERR_UNSUPPORTED, "%s: device ordinal %d above %d", what, dev, kMaxDevices - 1);
+  std::lock_guard<std::mutex> lock(cache.mu);
+  if (!cache.addr[dev]) {
+    void* addr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&addr, symbol);
+    if (e != cudaSuccess || !addr)
+      return fail(ESA_ERR_CUDA, "%s: cudaGetSymbolAddress failed: %s", what, cudaGetErrorString(e));
+    cache.addr[dev] = addr;
+  }
+  *out = cache.addr[dev];
+  return ESA_OK;
+}
+
+// The error word the kernels of a call record ESA_DEVERR_* bits in (one per
+// device; sticky until esa_device_errors resets it).
+static __device__ int g_device_errors;
+
+int device_error_word(int** out) {
+  static SymbolAddresses cache;
+  void* a = nullptr;
+  if (int rc = symbol_address(&g_device_errors, cache, "device error word", &a)) return rc;
+  *out = static_cast<int*>(a);
+  return ESA_OK;
+}
+
+// Up to this many (batch, head, row) pairs the forward runs the latency kernel
+// (one CTA per pair, slots split over warps) instead of a throughput kernel.
+constexpr int64_t kDecodeMaxPairs = 4096;
+
 template <typename K>
 int prepare_smem(K kernel, size_t bytes) {
   if (bytes > 48 * 1024) {
@@ -239,6 +283,11 @@ int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
     const int ht = window_heads<T, D>(p, p.alpha_zero, p.flags);
     if (ht == 4) return launch_window<T, 4>(p, s);
     if (ht == 2) return launch_window<T, 2>(p, s);
+  }
+  if ((int64_t)p.B * p.Hq * p.n_rows <= kDecodeMaxPairs && !needs_gather(p)) {
+    const int nw = std::min((p.pat.w + 31) >> 5, esa::kDecodeMaxWarps);
+    esa::fwd_decode_kernel<T, D><<<dim3(p.n_rows, p.Hq, p.B), nw * 32, 0, s>>>(p);
+    return check_launch("forward (decode)");
   }
   if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
     // slot-major tile kernel: 128 pairs per CTA share their K/V rows through L1
@@ -404,6 +453,20 @@ int esa_pattern_audit(int32_t num_heads, int32_t attn_length, int32_t layer_idx,
   return check_launch("esa_pattern_audit");
 }
 
+int esa_device_errors(int32_t clear, int32_t* flags, void* stream) {
+  if (!flags) return fail(ESA_ERR_INVALID, "esa_device_errors: null flags pointer");
+  int* word = nullptr;
+  if (int rc = device_error_word(&word)) return rc;
+  int32_t host = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(&host, word, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(word, 0, sizeof(int32_t), s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail(ESA_ERR_CUDA, "esa_device_errors: %s", cudaGetErrorString(e));
+  *flags = host;
+  return ESA_OK;
+}
+
 int esa_forward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_tensor_t v,
                 esa_tensor_t o, float* lse, void* stream) {
   if (int rc = check_problem(pb)) return rc;
@@ -415,6 +478,7 @@ int esa_forward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_ten
   if (int rc = check_tensor("o", o, es)) return rc;
   if (!lse) return fail(ESA_ERR_INVALID, "lse: null pointer");
   esa::AttnParams p = base_params(pb);
+  if (int rc = device_error_word(&p.err)) return rc;
   set_tensor(q, p.q, p.sqb, p.sqh, p.sqs);
   set_tensor(k, p.k, p.skb, p.skh, p.sks);
   set_tensor(v, p.v, p.svb, p.svh, p.svs);
@@ -456,6 +520,7 @@ int esa_backward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_te
   if (reinterpret_cast<uintptr_t>(workspace) % 256)
     return fail(ESA_ERR_INVALID, "workspace must be 256-byte aligned");
   esa::AttnParams p = base_params(pb);
+  if (int rc = device_error_word(&p.err)) return rc;
   set_tensor(q, p.q, p.sqb, p.sqh, p.sqs);
   set_tensor(k, p.k, p.skb, p.skh, p.sks);
   set_tensor(v, p.v, p.svb, p.svh, p.svs);
@@ -489,30 +554,10 @@ namespace {
 // variable, not device memory); it uses the device address looked up below.
 static __device__ __align__(256) unsigned char g_noalloc_workspace[ESA_NOALLOC_WORKSPACE_BYTES];
 
-constexpr int kNoallocMaxDevices = 64;
-std::mutex g_noalloc_mutex;
-void* g_noalloc_addr[kNoallocMaxDevices] = {};
-
-// Device address of g_noalloc_workspace on the current device, looked up once
-// per device (cudaGetSymbolAddress with that device current) and cached.
+// Device address of g_noalloc_workspace on the current device.
 int noalloc_workspace_address(void** out) {
-  int dev = -1;
-  const cudaError_t de = cudaGetDevice(&dev);
-  if (de != cudaSuccess) return fail(ESA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(de));
-  if (dev < 0 || dev >= kNoallocMaxDevices)
-    return fail(ESA_ERR_UNSUPPORTED, "esa_backward_noalloc: device ordinal %d above %d", dev,
-                kNoallocMaxDevices - 1);
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_addr[dev]) {
-    void* addr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_workspace);
-    if (e != cudaSuccess || !addr)
-      return fail(ESA_ERR_CUDA, "esa_backward_noalloc: cudaGetSymbolAddress failed: %s",
-                  cudaGetErrorString(e));
-    g_noalloc_addr[dev] = addr;
-  }
-  *out = g_noalloc_addr[dev];
-  return ESA_OK;
+  static SymbolAddresses cache;
+  return symbol_address(g_noalloc_workspace, cache, "esa_backward_noalloc", out);
 }
 
 }  // namespace

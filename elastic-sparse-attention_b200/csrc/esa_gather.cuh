@@ -34,8 +34,18 @@ struct Layout {
   static_assert(LPR >= 1 && LPR <= 32 && (32 % LPR) == 0, "unsupported head_dim");
 };
 
+// Position of query row j: rows[j] (negative entries count back from kv_len,
+// like torch indexing of the reference's [:kv_len] slice), or row_offset + j.
+// -1 for an entry outside [-kv_len, kv_len): callers mask every slot of it.
 __device__ __forceinline__ int query_pos(const AttnParams& p, int j) {
-  return p.rows ? (int)p.rows[j] : p.row_offset + j;
+  if (!p.rows) return p.row_offset + j;
+  int64_t r = p.rows[j];
+  if (r < 0) r += p.kv_len;
+  if (r < 0 || r >= p.kv_len) {
+    if (p.err) atomicOr(p.err, kErrQueryRange);
+    return -1;
+  }
+  return (int)r;
 }
 
 // Fills sidx[0..wpad) with the k/v buffer row of each slot of a pair, -1 for
@@ -47,7 +57,7 @@ __device__ __forceinline__ void fill_slot_rows(const AttnParams& p, int pos, int
   const float omt = __fsub_rn(1.f, t);
   for (int k = lane; k < wpad; k += 32) {
     int row = -1;
-    if (k < p.pat.w) {
+    if (k < p.pat.w && pos >= 0) {
       const int raw = raw_index(rw, k, t, omt);
       if (raw <= pos) {                              // causal mask (:532)
         const int c = min(raw, p.kv_len - 1);        // clamp (:615)

@@ -55,7 +55,8 @@ __device__ __forceinline__ bool dropout_keep(const AttnParams& p, int pos, int b
 }
 
 enum ErrBits : int {
-  kErrKvRange = 1,  // an index fell outside the k/v rows handed to the launch
+  kErrKvRange = 1,     // an index fell outside the k/v rows handed to the launch
+  kErrQueryRange = 4,  // a rows[] entry outside [-kv_len, kv_len)
 };
 
 }  // namespace esa

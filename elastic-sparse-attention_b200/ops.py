@@ -5,6 +5,7 @@ allocates), then launches on the current CUDA stream of the input's device.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from dataclasses import dataclass
 
@@ -75,6 +76,25 @@ def pattern_audit(num_heads: int, spec: PatternSpec, seq_len: int, device: torch
     return int(count.item())
 
 
+def _on(dev: torch.device):
+    """Make ``dev`` current for a library call (no-op when it already is)."""
+    return contextlib.nullcontext() if dev.index == torch.cuda.current_device() \
+        else torch.cuda.device(dev)
+
+
+def device_errors(device=None, clear: bool = True) -> int:
+    """ESA_DEVERR_* bits the kernels recorded on ``device`` (default: the
+    current device) since the last reset, after the work queued so far on its
+    current stream; resets them when ``clear``.  Synchronises that stream."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    flags = ctypes.c_int32(0)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.esa_device_errors(1 if clear else 0, ctypes.byref(flags),
+                                         _lib.stream_handle(dev)), "esa_device_errors")
+    return int(flags.value)
+
+
 def _problem(q, k, spec: PatternSpec, scale: float, rows, row_offset: int, kv_len: int,
              kv_offset: int, flags: int = 0, dropout_p: float = 0.0, dropout_seed: int = 0,
              weights=None):
@@ -107,7 +127,7 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: PatternSpec
                   kv_offset, _lib.FLAG_GATHER_ONLY if gather_only else 0, dropout_p,
                   dropout_seed, weights)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.check(lib.esa_forward(ctypes.byref(pb), _lib.tensor4(q), _lib.tensor4(k),
                                    _lib.tensor4(v), _lib.tensor4(out), lse.data_ptr(),
                                    _lib.stream_handle(dev)), "esa_forward")

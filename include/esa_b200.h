@@ -57,7 +57,13 @@ typedef struct {
  *   q_len, kv_len      -- query_states.shape[2], key_states.shape[2]
  *   rows               -- cache_position (:602-608) as device int64 [q_len],
  *                         or NULL: query row j is position row_offset + j
- *                         (the reference slices rows [:q_len], i.e. offset 0)
+ *                         (the reference slices rows [:q_len], i.e. offset 0).
+ *                         esa_forward reads a negative entry as kv_len + entry
+ *                         (torch indexing of the reference's [:kv_len] slice,
+ *                         :607-608); an entry outside [-kv_len, kv_len) gets
+ *                         an output row of zeros and sets
+ *                         ESA_DEVERR_QUERY_RANGE (no host round trip checks
+ *                         it).  esa_backward expects entries in [0, kv_len).
  *   kv_offset, kv_rows -- the k/v (and dk/dv) buffers hold positions
  *                         [kv_offset, kv_offset + kv_rows); for a plain call
  *                         kv_offset = 0 and kv_rows = kv_len
@@ -99,11 +105,29 @@ typedef struct {
  * tensor-core sliding-window kernel would apply (for cross-checking paths). */
 #define ESA_FLAG_GATHER_ONLY 1
 
+/* Bits of the per-device error word that kernels set instead of faulting
+ * (read and reset with esa_device_errors). */
+#define ESA_DEVERR_KV_RANGE 1     /* a computed key row fell outside the k/v buffer
+                                     (kv_offset / kv_rows too small); masked */
+#define ESA_DEVERR_TIMEOUT 2      /* a bounded wait of the tensor-core kernel gave
+                                     up; its tile was not written */
+#define ESA_DEVERR_QUERY_RANGE 4  /* a rows[] entry outside [-kv_len, kv_len);
+                                     its output row is zero */
+
 /* Library version, e.g. 100 for 0.1.0. */
 int esa_version(void);
 
 /* Message of the last failing call on this thread ("" if none). */
 const char* esa_last_error(void);
+
+/*
+ * Error bits (ESA_DEVERR_*) recorded by kernels on the current device since
+ * the last reset, as of the work queued on `stream` so far: copies the word
+ * to *flags after that work, resets it when clear != 0, and synchronises
+ * `stream`.  The reference has no counterpart (its kernels have no error
+ * channel; an out-of-range cache_position there is an indexing failure).
+ */
+int esa_device_errors(int32_t clear, int32_t* flags, void* stream);
 
 /*
  * Pattern buffers, bit-exact with the reference: idx/mask int64 [H, n_rows, w]

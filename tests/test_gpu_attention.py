@@ -167,11 +167,33 @@ def test_decode_cache_position(esa, cache_position):
 
 
 def test_cache_position_out_of_range(esa):
-    m = esa.ElasticSparseAttention(0, 4, 2, 32, 16, 64)
-    q = torch.randn(1, 2, 1, 32, device=DEV)
+    """Host cache_position and calls that need a backward raise IndexError
+    like the reference; a device cache_position under no_grad is not read
+    back: its out-of-range rows come out zero and set ESA_DEVERR_QUERY_RANGE."""
+    m = esa.ElasticSparseAttention(3, 4, 2, 32, 16, 64)
+    q = torch.randn(1, 2, 3, 32, device=DEV)
     k = torch.randn(1, 2, 10, 32, device=DEV)
+    esa.ops.device_errors()
     with pytest.raises(IndexError):
-        m(q, k, k, cache_position=torch.tensor([10], device=DEV))
+        m(q, k, k, cache_position=torch.tensor([10, 0, 1]))
+    with pytest.raises(IndexError):
+        m(q.requires_grad_(True), k, k, cache_position=torch.tensor([1, -11, 2], device=DEV))
+    q = q.detach()
+    with torch.no_grad():
+        good, _ = m(q, k, k, cache_position=torch.tensor([9, 4, -3], device=DEV))
+        assert esa.ops.device_errors() == 0
+        out, _ = m(q, k, k, cache_position=torch.tensor([9, 10, -3], device=DEV))
+        assert esa.ops.device_errors() == esa._lib.DEVERR_QUERY_RANGE
+        assert esa.ops.device_errors() == 0   # reset by the previous read
+        out2, _ = m(q, k, k, cache_position=torch.tensor([-11, 4, 7], device=DEV))
+        assert esa.ops.device_errors(clear=False) == esa._lib.DEVERR_QUERY_RANGE
+        assert esa.ops.device_errors() == esa._lib.DEVERR_QUERY_RANGE
+    assert torch.equal(out[:, 0], good[:, 0]) and torch.equal(out[:, 2], good[:, 2])
+    assert torch.count_nonzero(out[:, 1]) == 0 and torch.count_nonzero(out2[:, 0]) == 0
+    assert torch.equal(out2[:, 1], good[:, 1])
+    # a negative device position wraps in the kernel like torch indexing
+    ref = run_oracle(q, k, k, q, 3, 4, 16, cache_position=torch.tensor([9, 4, 7], device=DEV))[0]
+    assert_close(good.view(1, 3, 2, 32).transpose(1, 2), ref, torch.float32, "wrapped rows")
 
 
 def test_prefill_shorter_than_cache(esa):
@@ -300,7 +322,7 @@ def test_tile_forward_matches_gather_forward(esa, dtype, G, w, D, L, layer):
     """The slot-major tile forward (16-bit data, w <= 64) against the per-pair
     gather forward and the fp32 oracle, including odd w and ragged tiles."""
     g = torch.Generator().manual_seed(G * 31 + w + D)
-    Hkv = 2
+    Hkv = max(2, 8 // G)   # > 4096 (row, head) pairs: above the latency kernel's range
     Hq = Hkv * G
     q = randn(1, Hq, L, D, dtype=dtype, gen=g)
     k, v = randn(1, Hkv, L, D, dtype=dtype, gen=g), randn(1, Hkv, L, D, dtype=dtype, gen=g)
@@ -385,3 +407,31 @@ def test_dropout_matches_oracle_with_same_mask(esa, dtype, p):
     o_tri, w_tri = esa.ElasticSparseAttention(layer, 8, Hq, D, 64, L, num_key_value_heads=Hkv,
                                               attention_dropout=p).train()(q, k, v)
     assert w_tri is None and torch.allclose(o_eval.float(), o_tri.float(), atol=2e-2)
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.float32, 128), (torch.float32, 8), (torch.bfloat16, 256),
+                                     (torch.bfloat16, 128), (torch.float16, 64), (torch.bfloat16, 16)])
+@pytest.mark.parametrize("w,layer,nl", [(64, 7, 8), (5, 2, 4), (300, 3, 8), (32, 0, 8), (1000, 5, 6)])
+def test_decode_kernel_matches_gather_and_oracle(esa, dtype, D, w, layer, nl):
+    """Few-pair forwards (decode rows) run the latency kernel, whose slots are
+    split over the warps of a CTA (several sub-chunks per warp once w > 256):
+    against the per-pair gather kernel and the fp32 oracle, output and lse."""
+    g = torch.Generator().manual_seed(w + D)
+    B, Hq, Hkv, L = 2, 8, 2, 1500
+    rows = [L - 1, 0, 777, 31, 1499, 1200]
+    q = randn(B, Hq, len(rows), D, dtype=dtype, gen=g)
+    k, v = randn(B, Hkv, L, D, dtype=dtype, gen=g), randn(B, Hkv, L, D, dtype=dtype, gen=g)
+    spec = esa.PatternSpec(layer, nl, w)
+    rt = torch.tensor(rows, device=DEV)
+    o_d, lse_d = esa.ops.forward(q, k, v, spec, D ** -0.5, rows=rt)
+    o_g, lse_g = esa.ops.forward(q, k, v, spec, D ** -0.5, rows=rt, gather_only=True)
+    # the gather kernel sums weights rounded to the input type, this one fp32 weights
+    lse_tol = 1e-4 if dtype == torch.float32 else 1e-2
+    assert (lse_d - lse_g).abs().max().item() < lse_tol
+    idx, mask, _ = pattern.prepared_indices(Hq, w, layer, nl, L, len(rows), L, np.array(rows))
+    ti, tm = torch.from_numpy(idx).to(DEV), torch.from_numpy(mask).to(DEV)
+    ro, _ = naive.naive_forward(q.float(), k.float(), v.float(), ti, tm, D ** -0.5, Hq // Hkv)
+    assert_close(o_d, ro, dtype, f"decode {dtype} D{D} w{w}")
+    assert_close(o_g, ro, dtype, f"gather {dtype} D{D} w{w}")
+    lse_ref = naive.lse_rows(q, k, ti, tm, D ** -0.5, Hq // Hkv)
+    assert (lse_d.double() / 1.4426950408889634 - lse_ref).abs().max().item() < lse_tol

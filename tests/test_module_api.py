@@ -47,3 +47,19 @@ def test_q_longer_than_kv_needs_cache_position(esa):
 def test_pattern_spec(esa):
     s = esa.PatternSpec(3, 8, 64)
     assert (s.layer_idx, s.num_hidden_layers, s.attention_length) == (3, 8, 64)
+
+
+def test_prepare_rows_host_checks(esa):
+    """cache_position on the host: negative entries wrap (torch indexing of the
+    reference's [:kv_len] slice), out-of-range entries raise IndexError, a
+    wrong count raises ValueError -- all without a GPU."""
+    prep = esa.ElasticSparseAttention._prepare_rows
+    rows = prep(torch.tensor([5, -1, 0]), 3, 10, "cpu")
+    assert rows.tolist() == [5, 9, 0] and rows.dtype == torch.int64
+    assert prep([3, 4], 2, 10, "cpu").tolist() == [3, 4]
+    with pytest.raises(IndexError):
+        prep(torch.tensor([10]), 1, 10, "cpu")
+    with pytest.raises(IndexError):
+        prep(torch.tensor([-11]), 1, 10, "cpu")
+    with pytest.raises(ValueError):
+        prep(torch.tensor([1, 2]), 3, 10, "cpu")
