@@ -467,6 +467,67 @@ def bench_c5(args, world, rank, local):
             "clocks": clocks.summary()}
 
 
+def bench_c4(args):
+    """C4: the 4-layer decoder stack (hidden 4096, 32 heads of 128, SwiGLU
+    11008, RMSNorm, RoPE base 10000, vocabulary 32000, elastic sparse
+    attention with num_hidden_layers=4 and attention_length=64 in every
+    layer), B=1, L=262144 random token ids, random N(0, 0.02) bf16 weights;
+    one step = forward (mean next-token loss) + backward.  Metric: tokens/s."""
+    import elastic_sparse_attention_b200 as esa
+    dev = torch.device("cuda", 0)
+    L4 = args.c4_seq_len
+    m = esa.ElasticDecoderStack(max_seq_len=L4, device=dev, seed=0,
+                                activation_checkpointing=args.checkpoint)
+    g = torch.Generator().manual_seed(4)
+    ids_host = torch.randint(0, 32000, (1, L4), generator=g).pin_memory()
+    ids = ids_host.to(dev)
+
+    def step(inputs):
+        m.zero_grad(set_to_none=True)
+        loss = m(inputs, labels=inputs)
+        loss.backward()
+        return loss
+
+    for _ in range(max(args.warmup, 3)):
+        step(ids)
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(dev)
+    s_ = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        e0.record(s_)
+        for _ in range(args.steps):
+            loss = step(ids)
+        e1.record(s_)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    peak_gb = torch.cuda.max_memory_allocated(dev) / 1e9
+    # end to end: token ids from pinned host memory, loss read back every step
+    e0.record(s_)
+    for _ in range(args.steps):
+        loss_val = float(step(ids_host.to(dev, non_blocking=True)).item())
+    e1.record(s_)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    gemm_tflops = m.flops_per_token(L4) * L4 / (ms * 1e-3) / 1e12
+    return {"metric": "decoder-stack training tokens/s (fwd+bwd), C4", "value": round(L4 / (ms * 1e-3), 1),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: random token ids, N(0,0.02) weights",
+            "config": {"workload": "C4: 4 decoder layers, hidden 4096, 32 heads x 128, SwiGLU 11008, "
+                                   "RMSNorm, RoPE 1e4, vocab 32000, elastic attention w=64 nl=4",
+                       "global_batch": 1, "seq_len": L4,
+                       "activation_checkpointing": bool(args.checkpoint),
+                       "l2": "activations of GBs per step, far above the 126 MB L2"},
+            "loss": round(loss_val, 4), "peak_memory_gb": round(peak_gb, 1),
+            "gemm_flops_per_step": m.flops_per_token(L4) * L4,
+            "gemm_tflops_equiv": round(gemm_tflops, 1),
+            "e2e": {"value": round(L4 / (ms_e2e * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(ms_e2e, 2), "h2d_bytes_per_step": ids_host.numel() * 8,
+                    "d2h_bytes_per_step": 4},
+            "clocks": clocks.summary()}
+
+
 def bench_decode(args):
     """Decode latency (one GPU): one new token (or --decode-rows tokens) per
     sequence attends, through each of the 8 P8 layers, to its own K/V cache of
@@ -568,10 +629,13 @@ def profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["c3", "c5", "decode"], default="c3",
+    ap.add_argument("--workload", choices=["c3", "c4", "c5", "decode"], default="c3",
                     help="c5: the 1M-token sequence-sharded configuration; decode: "
                          "per-token latency against a 128k K/V cache")
     ap.add_argument("--decode-rows", type=int, default=1)
+    ap.add_argument("--c4-seq-len", type=int, default=262144)
+    ap.add_argument("--checkpoint", action="store_true",
+                    help="c4: recompute each decoder layer in the backward")
     ap.add_argument("--case", choices=["step", "one-layer"], default="step",
                     help="one-layer: a single fwd+bwd at --seq-len/--layer, for profilers")
     ap.add_argument("--seq-len", type=int, default=32768)
@@ -595,6 +659,9 @@ def main():
         return
     if args.workload == "decode":
         print(json.dumps(bench_decode(args)), flush=True)
+        return
+    if args.workload == "c4":
+        print(json.dumps(bench_c4(args)), flush=True)
         return
     world, rank, local = dist_init()
     if args.workload == "c5":

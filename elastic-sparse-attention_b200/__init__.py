@@ -5,11 +5,12 @@ HighCWu/elastic-sparse-attention.  Import it as ``elastic_sparse_attention_b200`
 (the loader module of that name at the repository root maps it to this
 directory).
 """
-from . import _lib, ops
+from . import _lib, layer_ops, ops
 from .attention import ElasticSparseAttention, ElasticSparseAttentionFunction
+from .decoder import ElasticDecoderStack
 from .ops import PatternSpec
 from .sharded import SequenceShardedElasticSparseAttention
 
-__all__ = ["ElasticSparseAttention", "ElasticSparseAttentionFunction", "PatternSpec",
-           "SequenceShardedElasticSparseAttention", "ops", "_lib"]
+__all__ = ["ElasticSparseAttention", "ElasticSparseAttentionFunction", "ElasticDecoderStack",
+           "PatternSpec", "SequenceShardedElasticSparseAttention", "layer_ops", "ops", "_lib"]
 __version__ = "0.1.0"

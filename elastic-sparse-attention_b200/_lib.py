@@ -23,7 +23,10 @@ DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 # Every symbol exported by include/esa_b200.h.
 EXPORTED = ("esa_version", "esa_last_error", "esa_device_errors", "esa_pattern",
             "esa_pattern_audit", "esa_forward", "esa_backward_workspace_size", "esa_backward",
-            "esa_backward_noalloc")
+            "esa_backward_noalloc",
+            # decoder-layer harness (include/esa_layer.h)
+            "esa_rmsnorm_forward", "esa_rmsnorm_backward_workspace_size", "esa_rmsnorm_backward",
+            "esa_rope_apply", "esa_swiglu_forward", "esa_swiglu_backward")
 
 # ESA_DEVERR_* bits of the per-device error word
 DEVERR_KV_RANGE = 1
@@ -90,6 +93,21 @@ def load() -> ctypes.CDLL:
                                      EsaTensor, P, EsaTensor, EsaTensor, EsaTensor, EsaTensor,
                                      P, P, P, ctypes.c_size_t, P]
         lib.esa_backward.restype = ctypes.c_int
+        F = ctypes.c_float
+        lib.esa_rmsnorm_forward.argtypes = [i32, i64, i32, P, P, P, P, F, P, P, P]
+        lib.esa_rmsnorm_forward.restype = ctypes.c_int
+        lib.esa_rmsnorm_backward_workspace_size.argtypes = [i64, i32]
+        lib.esa_rmsnorm_backward_workspace_size.restype = ctypes.c_size_t
+        lib.esa_rmsnorm_backward.argtypes = [i32, i64, i32, P, P, P, P, P, P, P, P,
+                                             ctypes.c_size_t, P]
+        lib.esa_rmsnorm_backward.restype = ctypes.c_int
+        lib.esa_rope_apply.argtypes = [i32, i32, i64, i32, EsaTensor, i32, EsaTensor, i32, P, P,
+                                       i32, P]
+        lib.esa_rope_apply.restype = ctypes.c_int
+        lib.esa_swiglu_forward.argtypes = [i32, i64, i32, P, P, P]
+        lib.esa_swiglu_forward.restype = ctypes.c_int
+        lib.esa_swiglu_backward.argtypes = [i32, i64, i32, P, P, P, P, P]
+        lib.esa_swiglu_backward.restype = ctypes.c_int
         _lib = lib
     return _lib
 

@@ -15,8 +15,10 @@
 #include <string>
 
 #include "esa_b200.h"
+#include "esa_layer.h"
 #include "esa_decode.cuh"
 #include "esa_gather.cuh"
+#include "esa_layer.cuh"
 #include "esa_pattern.cuh"
 #include "esa_window_tc.cuh"
 
@@ -581,3 +583,169 @@ extern "C" int esa_backward_noalloc(const esa_problem_t* pb, esa_tensor_t q, esa
   return esa_backward(pb, q, k, v, o, lse, dout, dq, dk, dv, sorted_rows, row_perm, ws,
                       ESA_NOALLOC_WORKSPACE_BYTES, stream);
 }
+
+// ---------------------------------------------------------------------------
+// Decoder-layer harness entry points (include/esa_layer.h).
+// ---------------------------------------------------------------------------
+namespace {
+
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+int check_rows_op(const char* what, int32_t dtype, int64_t n_rows, int32_t dim) {
+  if (dtype != ESA_DTYPE_F32 && dtype != ESA_DTYPE_BF16 && dtype != ESA_DTYPE_F16)
+    return fail(ESA_ERR_INVALID, "%s: unknown dtype %d", what, dtype);
+  if (n_rows < 0 || dim < 1) return fail(ESA_ERR_INVALID, "%s: bad shape", what);
+  const int es = elem_size(dtype);
+  if ((dim * es) % 16) return fail(ESA_ERR_INVALID, "%s: dim * element size must be a multiple of 16 bytes", what);
+  return ESA_OK;
+}
+
+template <typename F>
+int by_dtype(int32_t dtype, F&& f) {
+  switch (dtype) {
+    case ESA_DTYPE_F32: return f(float{});
+    case ESA_DTYPE_BF16: return f(__nv_bfloat16{});
+    default: return f(__half{});
+  }
+}
+
+int norm_threads(int32_t dtype, int32_t dim) {
+  const int vecs = dim / (16 / elem_size(dtype));
+  return (vecs + 31) / 32 * 32;
+}
+
+int64_t norm_grid(int64_t n_rows) {
+  const int64_t need = (n_rows + esa::layer::kNormRows - 1) / esa::layer::kNormRows;
+  return std::max<int64_t>(1, std::min<int64_t>(need, esa::layer::kNormBwdCtas));
+}
+
+}  // namespace
+
+extern "C" {
+
+int esa_rmsnorm_forward(int32_t dtype, int64_t n_rows, int32_t dim, const void* x,
+                        const void* residual, void* h_out, const void* weight, float eps,
+                        void* y, float* rstd, void* stream) {
+  if (int rc = check_rows_op("esa_rmsnorm_forward", dtype, n_rows, dim)) return rc;
+  if (norm_threads(dtype, dim) > 1024)
+    return fail(ESA_ERR_UNSUPPORTED, "esa_rmsnorm_forward: dim %d too large", dim);
+  if (n_rows == 0) return ESA_OK;
+  if (!x || !weight || !y || !rstd || (residual && !h_out))
+    return fail(ESA_ERR_INVALID, "esa_rmsnorm_forward: null pointer");
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(y) || (residual && !aligned16(residual)) ||
+      (h_out && !aligned16(h_out)))
+    return fail(ESA_ERR_INVALID, "esa_rmsnorm_forward: pointers must be 16-byte aligned");
+  const int threads = norm_threads(dtype, dim);
+  const int64_t grid = std::min<int64_t>((n_rows + esa::layer::kNormRows - 1) / esa::layer::kNormRows,
+                                         148 * 8);
+  return by_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    esa::layer::rmsnorm_fwd_kernel<T><<<(unsigned)grid, threads, 0, (cudaStream_t)stream>>>(
+        n_rows, dim, static_cast<const T*>(x), static_cast<const T*>(residual),
+        static_cast<T*>(h_out), static_cast<const T*>(weight), eps, static_cast<T*>(y), rstd);
+    return check_launch("esa_rmsnorm_forward");
+  });
+}
+
+size_t esa_rmsnorm_backward_workspace_size(int64_t n_rows, int32_t dim) {
+  if (n_rows <= 0 || dim <= 0) return 0;
+  return (size_t)norm_grid(n_rows) * dim * sizeof(float);
+}
+
+int esa_rmsnorm_backward(int32_t dtype, int64_t n_rows, int32_t dim, const void* h,
+                         const void* weight, const float* rstd, const void* dy,
+                         const void* dh_in, void* dh, void* dweight, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (int rc = check_rows_op("esa_rmsnorm_backward", dtype, n_rows, dim)) return rc;
+  if (norm_threads(dtype, dim) > 1024)
+    return fail(ESA_ERR_UNSUPPORTED, "esa_rmsnorm_backward: dim %d too large", dim);
+  if (n_rows == 0) return ESA_OK;
+  if (!h || !weight || !rstd || !dy || !dh || !dweight)
+    return fail(ESA_ERR_INVALID, "esa_rmsnorm_backward: null pointer");
+  if (!aligned16(h) || !aligned16(weight) || !aligned16(dy) || !aligned16(dh) ||
+      (dh_in && !aligned16(dh_in)))
+    return fail(ESA_ERR_INVALID, "esa_rmsnorm_backward: pointers must be 16-byte aligned");
+  const size_t need = esa_rmsnorm_backward_workspace_size(n_rows, dim);
+  if (!workspace || workspace_bytes < need)
+    return fail(ESA_ERR_WORKSPACE, "esa_rmsnorm_backward: workspace of %zu bytes given, %zu needed",
+                workspace_bytes, need);
+  const int threads = norm_threads(dtype, dim);
+  const int grid = (int)norm_grid(n_rows);
+  float* part = static_cast<float*>(workspace);
+  return by_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    cudaStream_t s = (cudaStream_t)stream;
+    esa::layer::rmsnorm_bwd_kernel<T><<<grid, threads, 0, s>>>(
+        n_rows, dim, static_cast<const T*>(h), static_cast<const T*>(weight), rstd,
+        static_cast<const T*>(dy), static_cast<const T*>(dh_in), static_cast<T*>(dh), part);
+    if (int rc = check_launch("esa_rmsnorm_backward")) return rc;
+    esa::layer::sum_partials_kernel<T><<<(dim + 255) / 256, 256, 0, s>>>(
+        grid, dim, part, static_cast<T*>(dweight));
+    return check_launch("esa_rmsnorm_backward (weight sum)");
+  });
+}
+
+int esa_rope_apply(int32_t dtype, int32_t batch, int64_t seq_len, int32_t head_dim,
+                   esa_tensor_t q, int32_t num_q_heads, esa_tensor_t k, int32_t num_k_heads,
+                   const int64_t* positions, const float* inv_freq, int32_t inverse,
+                   void* stream) {
+  if (dtype != ESA_DTYPE_F32 && dtype != ESA_DTYPE_BF16 && dtype != ESA_DTYPE_F16)
+    return fail(ESA_ERR_INVALID, "esa_rope_apply: unknown dtype %d", dtype);
+  const int es = elem_size(dtype);
+  if (batch < 0 || seq_len < 0 || num_q_heads < 0 || num_k_heads < 0 || head_dim < 2 ||
+      ((head_dim / 2) * es) % 16 || head_dim % 2)
+    return fail(ESA_ERR_INVALID, "esa_rope_apply: bad shape (head_dim / 2 * element size must "
+                "be a multiple of 16 bytes)");
+  if (batch > 65535 || seq_len > kMaxPosition)
+    return fail(ESA_ERR_UNSUPPORTED, "esa_rope_apply: batch or seq_len too large");
+  if (batch == 0 || seq_len == 0 || num_q_heads + (k.data ? num_k_heads : 0) == 0) return ESA_OK;
+  if (!q.data || !inv_freq) return fail(ESA_ERR_INVALID, "esa_rope_apply: null pointer");
+  if (int rc = check_tensor("q", q, es)) return rc;
+  if (k.data)
+    if (int rc = check_tensor("k", k, es)) return rc;
+  const int nk = k.data ? num_k_heads : 0;
+  const size_t smem = (size_t)head_dim * sizeof(float);
+  dim3 grid((unsigned)seq_len, (unsigned)batch);
+  return by_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    esa::layer::rope_kernel<T><<<grid, 256, smem, (cudaStream_t)stream>>>(
+        head_dim, static_cast<T*>(q.data), q.stride_b, q.stride_h, q.stride_s, num_q_heads,
+        static_cast<T*>(k.data), k.stride_b, k.stride_h, k.stride_s, nk, positions, inv_freq,
+        inverse ? -1.f : 1.f);
+    return check_launch("esa_rope_apply");
+  });
+}
+
+int esa_swiglu_forward(int32_t dtype, int64_t n_rows, int32_t ffn, const void* gate_up,
+                       void* out, void* stream) {
+  if (int rc = check_rows_op("esa_swiglu_forward", dtype, n_rows, ffn)) return rc;
+  if (n_rows == 0) return ESA_OK;
+  if (!gate_up || !out || !aligned16(gate_up) || !aligned16(out))
+    return fail(ESA_ERR_INVALID, "esa_swiglu_forward: null or misaligned pointer");
+  const unsigned grid = (unsigned)std::min<int64_t>(n_rows, 148 * 16);
+  return by_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    esa::layer::swiglu_fwd_kernel<T><<<grid, 256, 0, (cudaStream_t)stream>>>(
+        n_rows, ffn, static_cast<const T*>(gate_up), static_cast<T*>(out));
+    return check_launch("esa_swiglu_forward");
+  });
+}
+
+int esa_swiglu_backward(int32_t dtype, int64_t n_rows, int32_t ffn, const void* gate_up,
+                        const void* dout, void* dgate_up, void* out_recomputed, void* stream) {
+  if (int rc = check_rows_op("esa_swiglu_backward", dtype, n_rows, ffn)) return rc;
+  if (n_rows == 0) return ESA_OK;
+  if (!gate_up || !dout || !dgate_up || !aligned16(gate_up) || !aligned16(dout) ||
+      !aligned16(dgate_up) || (out_recomputed && !aligned16(out_recomputed)))
+    return fail(ESA_ERR_INVALID, "esa_swiglu_backward: null or misaligned pointer");
+  const unsigned grid = (unsigned)std::min<int64_t>(n_rows, 148 * 16);
+  return by_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    esa::layer::swiglu_bwd_kernel<T><<<grid, 256, 0, (cudaStream_t)stream>>>(
+        n_rows, ffn, static_cast<const T*>(gate_up), static_cast<const T*>(dout),
+        static_cast<T*>(dgate_up), static_cast<T*>(out_recomputed));
+    return check_launch("esa_swiglu_backward");
+  });
+}
+
+}  // extern "C"

@@ -137,20 +137,25 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: PatternSpec
 def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
              rows: torch.Tensor | None = None, row_offset: int = 0, kv_len: int | None = None,
              kv_offset: int = 0, sorted_rows=None, row_perm=None, workspace=None,
-             dropout_p: float = 0.0, dropout_seed: int = 0):
+             dropout_p: float = 0.0, dropout_seed: int = 0, dq=None, dk=None, dv=None):
     """Backward pass.  Returns (dq, dk, dv) in the input dtype.  With dropout,
-    pass the forward's dropout_p and dropout_seed (the keep mask is rebuilt)."""
+    pass the forward's dropout_p and dropout_seed (the keep mask is rebuilt).
+    dq / dk / dv may be given as (strided) views to write the gradients into,
+    e.g. the q / k / v parts of one fused QKV gradient buffer."""
     dev = _check_device(q, k, v, o, lse, dout)
-    dq = torch.empty_like(q)
-    dk = torch.empty_like(k)
-    dv = torch.empty_like(v)
+    dq = torch.empty_like(q) if dq is None else dq
+    dk = torch.empty_like(k) if dk is None else dk
+    dv = torch.empty_like(v) if dv is None else dv
+    for g, ref in ((dq, q), (dk, k), (dv, v)):
+        if g.shape != ref.shape or g.dtype != ref.dtype or g.device != ref.device:
+            raise ValueError("gradient buffers must match the shapes and dtypes of q, k, v")
     pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
                   kv_offset, 0, dropout_p, dropout_seed)
     lib = _lib.load()
     need = lib.esa_backward_workspace_size(ctypes.byref(pb))
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.check(lib.esa_backward(ctypes.byref(pb), _lib.tensor4(q), _lib.tensor4(k),
                                     _lib.tensor4(v), _lib.tensor4(o), lse.data_ptr(),
                                     _lib.tensor4(dout), _lib.tensor4(dq), _lib.tensor4(dk),

@@ -11,12 +11,15 @@ import pytest
 from conftest import ROOT
 
 HEADER = os.path.join(ROOT, "include", "esa_b200.h")
+HEADERS = (HEADER, os.path.join(ROOT, "include", "esa_layer.h"))
 
 
 def header_functions():
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(esa_[a-z_0-9]+)\s*\(", text)))
+    names = set()
+    for path in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", open(path).read(), flags=re.S)
+        names |= set(re.findall(r"\b(esa_[a-z_0-9]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_library_exports_header_symbols(esa):

@@ -63,3 +63,27 @@ def test_prepare_rows_host_checks(esa):
         prep(torch.tensor([-11]), 1, 10, "cpu")
     with pytest.raises(ValueError):
         prep(torch.tensor([1, 2]), 3, 10, "cpu")
+
+
+def test_decoder_stack_builds_on_cpu(esa):
+    """The C4 harness module: parameter shapes, initialisation and the GEMM
+    FLOP count (its kernels need a GPU; construction does not)."""
+    m = esa.ElasticDecoderStack(vocab_size=100, hidden_size=64, num_hidden_layers=2,
+                                num_attention_heads=4, num_key_value_heads=2,
+                                intermediate_size=96, attention_length=8, max_seq_len=32,
+                                dtype=torch.float32, device="cpu")
+    shapes = {n: tuple(p.shape) for n, p in m.named_parameters()}
+    assert shapes["layers.0.qkv_proj"] == ((4 + 2 * 2) * 16, 64)
+    assert shapes["layers.1.gate_up_proj"] == (2 * 96, 64)
+    assert shapes["lm_head"] == (100, 64)
+    assert torch.equal(m.final_norm, torch.ones(64))
+    assert 0.015 < m.embed.std().item() < 0.025
+    assert [s.layer_idx for s in m.specs] == [0, 1] and m.specs[0].num_hidden_layers == 2
+    per_layer = 64 * 128 + 64 * 64 + 3 * 64 * 96
+    assert m.flops_per_token(32) == 6.0 * (2 * per_layer + 100 * 64)
+    inv = esa.layer_ops.rope_inv_freq(16, 10000.0, "cpu")
+    assert torch.allclose(inv, 1.0 / 10000.0 ** (torch.arange(0, 16, 2).float() / 16))
+    with pytest.raises(ValueError):
+        esa.ElasticDecoderStack(hidden_size=64, num_attention_heads=4, num_key_value_heads=3,
+                                vocab_size=10, intermediate_size=8, dtype=torch.float32,
+                                device="cpu")
