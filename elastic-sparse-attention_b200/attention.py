@@ -75,10 +75,13 @@ class ElasticSparseAttentionFunction(torch.autograd.Function):
         if q.shape[1] != k.shape[1] * num_kv_groups:
             raise ValueError("num_kv_groups does not match the query / key head counts")
         q, k, v = (ops.as_kernel_operand(t) for t in (q, k, v))
+        # the forward's probabilities, kept for the backward where that path writes them
+        probs = ops.probs_buffer(q, k, pattern, rows=rows, dropout_p=dropout_p,
+                                 return_weights=return_weights)
         res = ops.forward(q, k, v, pattern, sm_scale, rows=rows, dropout_p=dropout_p,
-                          dropout_seed=dropout_seed, return_weights=return_weights)
+                          dropout_seed=dropout_seed, return_weights=return_weights, probs=probs)
         o, lse = res[0], res[1]
-        ctx.save_for_backward(q, k, v, o, lse, rows)
+        ctx.save_for_backward(q, k, v, o, lse, rows, probs)
         ctx.pattern = pattern
         ctx.sm_scale = sm_scale
         ctx.dropout = (dropout_p, dropout_seed)
@@ -89,7 +92,7 @@ class ElasticSparseAttentionFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, do, *unused):
-        q, k, v, o, lse, rows = ctx.saved_tensors
+        q, k, v, o, lse, rows, probs = ctx.saved_tensors
         do = ops.as_kernel_operand(do)
         spec = ctx.pattern
         sorted_rows = perm = None
@@ -101,7 +104,8 @@ class ElasticSparseAttentionFunction(torch.autograd.Function):
         _ensure_monotone(q.shape[1], spec, max(seq, 2), q.device)
         dq, dk, dv = ops.backward(q, k, v, o, lse, do, spec, ctx.sm_scale, rows=rows,
                                   sorted_rows=sorted_rows, row_perm=perm,
-                                  dropout_p=ctx.dropout[0], dropout_seed=ctx.dropout[1])
+                                  dropout_p=ctx.dropout[0], dropout_seed=ctx.dropout[1],
+                                  probs=probs)
         return dq, dk, dv, None, None, None, None, None, None, None
 
 

@@ -104,6 +104,8 @@ int check_problem(const esa_problem_t* pb) {
     return fail(ESA_ERR_INVALID, "dropout_p must be in [0, 1]");
   if (pb->weights && reinterpret_cast<uintptr_t>(pb->weights) % 4)
     return fail(ESA_ERR_INVALID, "weights must be 4-byte aligned");
+  if (pb->probs && reinterpret_cast<uintptr_t>(pb->probs) % 16)
+    return fail(ESA_ERR_INVALID, "probs must be 16-byte aligned");
   return ESA_OK;
 }
 
@@ -132,6 +134,7 @@ esa::AttnParams base_params(const esa_problem_t* pb) {
   }
   p.seed = pb->dropout_seed;
   p.weights = pb->weights;
+  p.probs = static_cast<float*>(pb->probs);
   return p;
 }
 
@@ -241,9 +244,9 @@ bool encode_map(CUtensorMap* m, const void* ptr, bool fp16, int64_t D, int64_t r
 
 // Heads per UMMA tile for the window path, 0 when the call is not eligible.
 template <typename T, int D>
-int window_heads(const esa::AttnParams& p, bool alpha_zero, int flags) {
+int window_heads_for_problem(const esa::AttnParams& p) {
   if (std::is_same<T, float>::value || D != esa::kWinHeadDim) return 0;
-  if (!alpha_zero || needs_gather(p) || p.rows) return 0;
+  if (!p.alpha_zero || needs_gather(p) || p.rows) return 0;
   const int ht = (p.G % 4 == 0) ? 4 : (p.G == 2 ? 2 : 0);
   if (!ht) return 0;
   const int qt = esa::kWinRows / ht;
@@ -254,10 +257,37 @@ int window_heads(const esa::AttnParams& p, bool alpha_zero, int flags) {
   if (p.kv_offset > std::max(0, p.row_offset - p.pat.w + 1) ||
       (int64_t)p.kv_offset + p.kv_rows < last)
     return 0;
+  return ht;
+}
+
+// The window kernel also needs positive strides (tensor maps) and the driver's
+// tensor-map encoder.
+template <typename T, int D>
+int window_heads(const esa::AttnParams& p, bool, int) {
+  const int ht = window_heads_for_problem<T, D>(p);
+  if (!ht) return 0;
   if (p.sqb <= 0 || p.sqh <= 0 || p.sqs <= 0 || p.skb <= 0 || p.skh <= 0 || p.sks <= 0 ||
       p.svb <= 0 || p.svh <= 0 || p.svs <= 0)
     return 0;
   return tmap_encoder() ? ht : 0;
+}
+
+// The slot-major tile forward / query-side backward apply (16-bit data,
+// head_dim 64 or 128, w <= 64, G divides 128, consecutive positions, at least
+// 256 rows, no dropout / weights output, more pairs than the latency kernel
+// takes).  Only this forward writes `probs`.
+template <typename T, int D>
+bool tile_path(const esa::AttnParams& p) {
+  if constexpr (std::is_same<T, float>::value || !(D == 64 || D == 128)) {
+    return false;
+  } else {
+    return p.pat.w <= esa::kTileMaxW && p.G <= esa::kTilePairs && esa::kTilePairs % p.G == 0 &&
+           !p.rows && p.n_rows >= 256 && !needs_gather(p);
+  }
+}
+
+bool decode_path(const esa::AttnParams& p) {
+  return (int64_t)p.B * p.Hq * p.n_rows <= kDecodeMaxPairs && !needs_gather(p);
 }
 
 template <typename T, int HT>
@@ -279,6 +309,15 @@ int launch_window(const esa::AttnParams& p, cudaStream_t s) {
   return check_launch("forward (tensor-core window)");
 }
 
+// Whether esa_forward for this call runs the tile kernel, the only one that
+// writes `probs` (and so whether the backward may read them).
+template <typename T, int D>
+bool forward_writes_probs(const esa::AttnParams& p) {
+  if (window_heads<T, D>(p, p.alpha_zero, p.flags)) return false;
+  if (decode_path(p)) return false;
+  return tile_path<T, D>(p);
+}
+
 template <typename T, int D>
 int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
   if constexpr (!std::is_same<T, float>::value && D == esa::kWinHeadDim) {
@@ -286,15 +325,14 @@ int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
     if (ht == 4) return launch_window<T, 4>(p, s);
     if (ht == 2) return launch_window<T, 2>(p, s);
   }
-  if ((int64_t)p.B * p.Hq * p.n_rows <= kDecodeMaxPairs && !needs_gather(p)) {
+  if (decode_path(p)) {
     const int nw = std::min((p.pat.w + 31) >> 5, esa::kDecodeMaxWarps);
     esa::fwd_decode_kernel<T, D><<<dim3(p.n_rows, p.Hq, p.B), nw * 32, 0, s>>>(p);
     return check_launch("forward (decode)");
   }
   if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
     // slot-major tile kernel: 128 pairs per CTA share their K/V rows through L1
-    if (p.pat.w <= esa::kTileMaxW && p.G <= esa::kTilePairs && esa::kTilePairs % p.G == 0 &&
-        !p.rows && p.n_rows >= 256 && !needs_gather(p)) {
+    if (tile_path<T, D>(p)) {
       const int tq = esa::kTilePairs / p.G;
       dim3 grid((p.n_rows + tq - 1) / tq, p.Hkv, p.B);
       auto kern = esa::fwd_tile_kernel<T, D>;
@@ -314,11 +352,13 @@ int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
 }
 
 template <typename T, int D>
-int launch_backward(const esa::AttnParams& p, cudaStream_t s) {
+int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
+  // probabilities from the forward only where that forward wrote them
+  esa::AttnParams p = p_in;
+  if (p.probs && !forward_writes_probs<T, D>(p)) p.probs = nullptr;
   bool query_done = false;
   if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
-    if (p.n_rows > 0 && p.pat.w <= esa::kTileMaxW && p.G <= esa::kTilePairs &&
-        esa::kTilePairs % p.G == 0 && !p.rows && p.n_rows >= 256 && !needs_gather(p)) {
+    if (p.n_rows > 0 && tile_path<T, D>(p)) {
       const int tq = esa::kTilePairs / p.G;
       dim3 grid((p.n_rows + tq - 1) / tq, p.Hkv, p.B);
       auto kern = esa::bwd_query_tile_kernel<T, D>;
@@ -355,6 +395,14 @@ int launch_backward(const esa::AttnParams& p, cudaStream_t s) {
   return ESA_OK;
 }
 
+struct ProbsQuery {
+  template <typename T, int D>
+  static int run(const esa::AttnParams& p, cudaStream_t) {
+    if (window_heads_for_problem<T, D>(p)) return 0;
+    if (decode_path(p)) return 0;
+    return tile_path<T, D>(p) ? 1 : 0;
+  }
+};
 struct FwdOp {
   template <typename T, int D>
   static int run(const esa::AttnParams& p, cudaStream_t s) { return launch_forward<T, D>(p, s); }
@@ -453,6 +501,13 @@ int esa_pattern_audit(int32_t num_heads, int32_t attn_length, int32_t layer_idx,
   esa::audit_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(P, (int)seq_len,
                                                                             d_count);
   return check_launch("esa_pattern_audit");
+}
+
+int esa_forward_writes_probs(const esa_problem_t* pb) {
+  if (int rc = check_problem(pb)) return rc;
+  if (pb->q_len == 0 || pb->batch == 0) return 0;
+  const esa::AttnParams p = base_params(pb);
+  return dispatch_op<ProbsQuery>(pb->dtype, pb->head_dim, p, nullptr);
 }
 
 int esa_device_errors(int32_t clear, int32_t* flags, void* stream) {

@@ -333,6 +333,23 @@ fwd_tile_kernel(const AttnParams p) {
   }
   __syncthreads();
 
+  // ---- optional: the normalised probabilities for the backward, slot-major
+  // [B, Hq, w, n]; warp per (head, slot), lanes over consecutive queries so
+  // every store instruction writes whole 128-byte lines ----------------------
+  if (p.probs) {
+    for (int hk = warp; hk < G * w; hk += 8) {
+      const int hl = hk / w;
+      const int k = hk - hl * w;
+      float* dst = p.probs + (((int64_t)b * p.Hq + hkv * G + hl) * w + k) * p.n_rows + j0;
+      for (int jl = lane; jl < TQ; jl += 32) {
+        if (j0 + jl >= p.n_rows) break;
+        const int pi = jl * G + hl;
+        const float lm = sl[pi];
+        dst[jl] = lm > 0.f ? M::to_float(sp[pi][k]) / lm : 0.f;
+      }
+    }
+  }
+
   // ---- O = P V: lane keeps the EPL output dims r*EPL.. of its MI pairs ----
   float acc[MI][EPL];
 #pragma unroll
@@ -447,8 +464,19 @@ bwd_query_tile_kernel(const AttnParams p) {
                  : make_uint4(0, 0, 0, 0);
   };
 
-  // ---- pass 1a: p = exp2(s * scale_log2 - lse) ----------------------------
-  {
+  // ---- pass 1a: p = exp2(s * scale_log2 - lse), or the forward's p --------
+  if (p.probs) {
+    for (int hk = warp; hk < G * w; hk += 8) {
+      const int hl = hk / w;
+      const int k = hk - hl * w;
+      const float* src = p.probs + (((int64_t)b * p.Hq + hkv * G + hl) * w + k) * n + j0;
+      for (int jl = lane; jl < TQ; jl += 32) {
+        if (j0 + jl >= n) break;
+        sprob[jl * G + hl][k] = src[jl];
+      }
+    }
+    __syncthreads();
+  } else {
     const float lse2 = my_live ? p.lse[((int64_t)b * p.Hq + my_h) * n + my_j] : 0.f;
     uint4 qv[MI];
 #pragma unroll

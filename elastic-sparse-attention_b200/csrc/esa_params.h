@@ -45,6 +45,7 @@ struct AttnParams {
   float keep_scale;            // 1 / (1 - dropout_p)
   uint64_t seed;
   void* weights;               // optional [B, Hq, n_rows, w] weights output (input dtype)
+  float* probs;                // optional fp32 [B, Hq, w, n_rows] probabilities (tile path)
 };
 
 __device__ __forceinline__ bool dropout_keep(const AttnParams& p, int pos, int bh, int k) {

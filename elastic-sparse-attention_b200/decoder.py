@@ -85,16 +85,17 @@ class _AttentionBlock(torch.autograd.Function):
         q, k, v = _split_heads(qkv, B, L, Hq, Hkv, D)
         layer_ops.rope_(q, k, inv_freq, positions)
         scale = D ** -0.5
-        o, lse = ops.forward(q, k, v, spec, scale)            # o: view of [B, L, Hq, D]
+        probs = ops.probs_buffer(q, k, spec)                  # kept for the backward
+        o, lse = ops.forward(q, k, v, spec, scale, probs=probs)   # o: view of [B, L, Hq, D]
         o_rows = o.transpose(1, 2).reshape(B, L, Hq * D)      # a view, no copy
         a = torch.matmul(o_rows, wo.t())
-        ctx.save_for_backward(y, wqkv, wo, qkv, o_rows, lse, inv_freq, positions)
+        ctx.save_for_backward(y, wqkv, wo, qkv, o_rows, lse, inv_freq, positions, probs)
         ctx.meta = (spec, heads, scale)
         return a
 
     @staticmethod
     def backward(ctx, da):
-        y, wqkv, wo, qkv, o_rows, lse, inv_freq, positions = ctx.saved_tensors
+        y, wqkv, wo, qkv, o_rows, lse, inv_freq, positions, probs = ctx.saved_tensors
         spec, (Hq, Hkv, D), scale = ctx.meta
         B, L, d = y.shape
         da = da.contiguous()
@@ -106,7 +107,7 @@ class _AttentionBlock(torch.autograd.Function):
         dq, dk, dv = _split_heads(dqkv, B, L, Hq, Hkv, D)
         _ensure_monotone(Hq, spec, max(L, 2), y.device)
         ops.backward(q, k, v, o, lse, do_rows.view(B, L, Hq, D).transpose(1, 2), spec, scale,
-                     dq=dq, dk=dk, dv=dv)
+                     dq=dq, dk=dk, dv=dv, probs=probs)
         del do_rows
         layer_ops.rope_(dq, dk, inv_freq, positions, inverse=True)
         dy = torch.matmul(dqkv, wqkv)

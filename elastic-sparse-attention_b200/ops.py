@@ -97,25 +97,43 @@ def device_errors(device=None, clear: bool = True) -> int:
 
 def _problem(q, k, spec: PatternSpec, scale: float, rows, row_offset: int, kv_len: int,
              kv_offset: int, flags: int = 0, dropout_p: float = 0.0, dropout_seed: int = 0,
-             weights=None):
+             weights=None, probs=None):
     B, Hq, Lq, D = q.shape
     return _lib.problem(dtype=q.dtype, batch=B, num_heads=Hq, num_kv_heads=k.shape[1], head_dim=D,
                         attn_length=spec.attention_length, layer_idx=spec.layer_idx,
                         num_hidden_layers=spec.num_hidden_layers, q_len=Lq, kv_len=kv_len,
                         kv_offset=kv_offset, kv_rows=k.shape[2], row_offset=row_offset,
                         rows=rows, scale=scale, flags=flags, dropout_p=dropout_p,
-                        dropout_seed=dropout_seed, weights=weights)
+                        dropout_seed=dropout_seed, weights=weights, probs=probs)
+
+
+def probs_buffer(q, k, spec: PatternSpec, rows: torch.Tensor | None = None, row_offset: int = 0,
+                 kv_len: int | None = None, kv_offset: int = 0, dropout_p: float = 0.0,
+                 return_weights: bool = False) -> torch.Tensor | None:
+    """A float32 [B, Hq, w, Lq] buffer for the forward to leave its softmax
+    probabilities in, so that the backward skips recomputing the scores; None
+    when the forward path for this problem does not write them."""
+    B, Hq, Lq, _ = q.shape
+    if return_weights or dropout_p > 0:
+        return None   # those run the gather kernels, which do not write probs
+    pb = _problem(q, k, spec, 1.0, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
+                  kv_offset)
+    if _lib.load().esa_forward_writes_probs(ctypes.byref(pb)) != 1:
+        return None
+    return torch.empty((B, Hq, spec.attention_length, Lq), dtype=torch.float32, device=q.device)
 
 
 def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: PatternSpec, scale: float,
             rows: torch.Tensor | None = None, row_offset: int = 0, kv_len: int | None = None,
             kv_offset: int = 0, out: torch.Tensor | None = None, gather_only: bool = False,
-            dropout_p: float = 0.0, dropout_seed: int = 0, return_weights: bool = False):
+            dropout_p: float = 0.0, dropout_seed: int = 0, return_weights: bool = False,
+            probs: torch.Tensor | None = None):
     """Forward pass.  Returns (o [B, Hq, Lq, D] as a view of a [B, Lq, Hq, D]
     buffer, lse float32 [B, Hq, Lq] base 2) and, with ``return_weights``, the
     softmax weights after dropout [B, Hq, Lq, w] in the input dtype.
     ``gather_only`` keeps sliding-window layers on the CUDA-core kernel (for
-    cross-checking the two paths)."""
+    cross-checking the two paths).  ``probs`` (from :func:`probs_buffer`)
+    receives the probabilities for :func:`backward`."""
     dev = _check_device(q, k, v)
     B, Hq, Lq, D = q.shape
     if out is None:
@@ -123,9 +141,11 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: PatternSpec
     lse = torch.empty((B, Hq, Lq), dtype=torch.float32, device=dev)
     weights = (torch.empty((B, Hq, Lq, spec.attention_length), dtype=q.dtype, device=dev)
                if return_weights else None)
+    if probs is not None:
+        _check_probs(probs, q, spec)
     pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
                   kv_offset, _lib.FLAG_GATHER_ONLY if gather_only else 0, dropout_p,
-                  dropout_seed, weights)
+                  dropout_seed, weights, probs)
     lib = _lib.load()
     with _on(dev):
         _lib.check(lib.esa_forward(ctypes.byref(pb), _lib.tensor4(q), _lib.tensor4(k),
@@ -137,7 +157,8 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spec: PatternSpec
 def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
              rows: torch.Tensor | None = None, row_offset: int = 0, kv_len: int | None = None,
              kv_offset: int = 0, sorted_rows=None, row_perm=None, workspace=None,
-             dropout_p: float = 0.0, dropout_seed: int = 0, dq=None, dk=None, dv=None):
+             dropout_p: float = 0.0, dropout_seed: int = 0, dq=None, dk=None, dv=None,
+             probs: torch.Tensor | None = None):
     """Backward pass.  Returns (dq, dk, dv) in the input dtype.  With dropout,
     pass the forward's dropout_p and dropout_seed (the keep mask is rebuilt).
     dq / dk / dv may be given as (strided) views to write the gradients into,
@@ -149,8 +170,10 @@ def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
     for g, ref in ((dq, q), (dk, k), (dv, v)):
         if g.shape != ref.shape or g.dtype != ref.dtype or g.device != ref.device:
             raise ValueError("gradient buffers must match the shapes and dtypes of q, k, v")
+    if probs is not None:
+        _check_probs(probs, q, spec)
     pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
-                  kv_offset, 0, dropout_p, dropout_seed)
+                  kv_offset, 0, dropout_p, dropout_seed, None, probs)
     lib = _lib.load()
     need = lib.esa_backward_workspace_size(ctypes.byref(pb))
     if workspace is None or workspace.numel() < need:
@@ -163,6 +186,14 @@ def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
                                     workspace.data_ptr(), workspace.numel(),
                                     _lib.stream_handle(dev)), "esa_backward")
     return dq, dk, dv
+
+
+def _check_probs(probs: torch.Tensor, q: torch.Tensor, spec: PatternSpec) -> None:
+    B, Hq, Lq, _ = q.shape
+    if (probs.dtype != torch.float32 or probs.shape != (B, Hq, spec.attention_length, Lq)
+            or not probs.is_contiguous() or probs.device != q.device):
+        raise ValueError("probs must be a contiguous float32 [B, Hq, w, q_len] tensor "
+                         "(see probs_buffer)")
 
 
 def backward_workspace_bytes(q, k, spec: PatternSpec, kv_len: int | None = None) -> int:

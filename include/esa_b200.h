@@ -77,6 +77,13 @@ typedef struct {
  *                         after dropout, input dtype, contiguous
  *                         [B, num_heads, q_len, attn_length] (the reference's
  *                         naive attn_weights, :673-680); NULL = not written
+ *   probs              -- optional float32 [B, num_heads, attn_length, q_len]
+ *                         (slot-major, contiguous, 16-byte aligned): when
+ *                         esa_forward_writes_probs(problem) is 1, esa_forward
+ *                         writes the normalised softmax probabilities there
+ *                         and esa_backward, given the same buffer, reads them
+ *                         instead of recomputing the scores (one gather pass
+ *                         less).  NULL = the backward recomputes them.
  */
 typedef struct {
   int32_t dtype;
@@ -99,6 +106,7 @@ typedef struct {
   int32_t reserved;
   uint64_t dropout_seed;
   void* weights;
+  void* probs;
 } esa_problem_t;
 
 /* flags: run every layer on the CUDA-core gather kernels, also where the
@@ -119,6 +127,14 @@ int esa_version(void);
 
 /* Message of the last failing call on this thread ("" if none). */
 const char* esa_last_error(void);
+
+/*
+ * 1 if esa_forward, for this problem, runs the kernel that writes `probs`
+ * (and esa_backward can use them), 0 if not, negative on an invalid problem.
+ * No reference counterpart: the reference recomputes the scores in its
+ * backward (:169-233) from the saved row statistics L and M.
+ */
+int esa_forward_writes_probs(const esa_problem_t* problem);
 
 /*
  * Error bits (ESA_DEVERR_*) recorded by kernels on the current device since

@@ -43,8 +43,8 @@ def test_struct_layout_matches_header(tmp_path, esa):
         " offsetof(esa_problem_t, q_len), offsetof(esa_problem_t, rows),"
         " offsetof(esa_problem_t, scale), sizeof(esa_tensor_t),"
         " offsetof(esa_tensor_t, stride_s), offsetof(esa_problem_t, row_offset));\n"
-        ' printf(" %zu %zu\\n", offsetof(esa_problem_t, dropout_seed),'
-        " offsetof(esa_problem_t, weights));\n"
+        ' printf(" %zu %zu %zu\\n", offsetof(esa_problem_t, dropout_seed),'
+        " offsetof(esa_problem_t, weights), offsetof(esa_problem_t, probs));\n"
         " return 0; }\n")
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-std=c99", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)],
@@ -53,7 +53,8 @@ def test_struct_layout_matches_header(tmp_path, esa):
                                           check=True).stdout.split()]
     P, T = esa._lib.EsaProblem, esa._lib.EsaTensor
     want = [ctypes.sizeof(P), P.q_len.offset, P.rows.offset, P.scale.offset, ctypes.sizeof(T),
-            T.stride_s.offset, P.row_offset.offset, P.dropout_seed.offset, P.weights.offset]
+            T.stride_s.offset, P.row_offset.offset, P.dropout_seed.offset, P.weights.offset,
+            P.probs.offset]
     assert got == want
 
 
@@ -62,7 +63,7 @@ def _problem(esa, **kw):
                 num_kv_heads=2, head_dim=128, attn_length=64, layer_idx=3, num_hidden_layers=8,
                 q_len=16, kv_len=16, kv_offset=0, kv_rows=16, row_offset=0, rows=None,
                 scale=128 ** -0.5, flags=0, dropout_p=0.0, reserved=0, dropout_seed=0,
-                weights=None)
+                weights=None, probs=None)
     base.update(kw)
     return esa._lib.EsaProblem(**base)
 
@@ -124,3 +125,19 @@ def test_pattern_rejects_bad_rows(esa):
     assert lib.esa_pattern(4, 64, 0, 8, 1 << 25, None, 0, 0, 16, 16, None) == -1
     assert lib.esa_pattern(4, 0, 0, 8, 16, None, 0, 0, 16, 16, None) == -1
     assert lib.esa_pattern(4, 64, 0, 8, 0, None, 0, 0, None, None, None) == 0
+
+
+@pytest.mark.parametrize("kw,want", [
+    (dict(), 0),                                          # 16 rows: the latency kernel
+    (dict(q_len=4096, kv_len=4096, kv_rows=4096), 1),     # tile kernel
+    (dict(q_len=4096, kv_len=4096, kv_rows=4096, layer_idx=0), 0),   # tensor-core window
+    (dict(q_len=4096, kv_len=4096, kv_rows=4096, dtype=0), 0),       # fp32: gather kernels
+    (dict(q_len=4096, kv_len=4096, kv_rows=4096, dropout_p=0.1), 0),
+    (dict(q_len=4096, kv_len=4096, kv_rows=4096, attn_length=65), 0),
+    (dict(num_kv_heads=3), -1),
+])
+def test_forward_writes_probs_query(esa, kw, want):
+    """Which forward paths leave their probabilities for the backward (a host
+    decision, no GPU needed)."""
+    lib = esa._lib.load()
+    assert lib.esa_forward_writes_probs(ctypes.byref(_problem(esa, **kw))) == want

@@ -435,3 +435,42 @@ def test_decode_kernel_matches_gather_and_oracle(esa, dtype, D, w, layer, nl):
     assert_close(o_g, ro, dtype, f"gather {dtype} D{D} w{w}")
     lse_ref = naive.lse_rows(q, k, ti, tm, D ** -0.5, Hq // Hkv)
     assert (lse_d.double() / 1.4426950408889634 - lse_ref).abs().max().item() < lse_tol
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("G,w,D,L,layer", [(4, 64, 128, 1000, 7), (2, 33, 64, 2100, 3),
+                                           (1, 64, 128, 700, 5), (8, 7, 128, 515, 2)])
+def test_saved_probs_forward_backward(esa, dtype, G, w, D, L, layer):
+    """The tile forward leaves the normalised probabilities (slot-major fp32)
+    for the backward, which then skips recomputing the scores: the
+    probabilities match the oracle's softmax weights, the forward outputs are
+    unchanged, and the gradients match both the recomputing backward and the
+    oracle."""
+    g = torch.Generator().manual_seed(G * 5 + w + L)
+    Hkv = max(2, 8 // G)
+    Hq = Hkv * G
+    q, do = randn(1, Hq, L, D, dtype=dtype, gen=g), randn(1, Hq, L, D, dtype=dtype, gen=g)
+    k, v = randn(1, Hkv, L, D, dtype=dtype, gen=g), randn(1, Hkv, L, D, dtype=dtype, gen=g)
+    spec = esa.PatternSpec(layer, 8, w)
+    scale = D ** -0.5
+    pr = esa.ops.probs_buffer(q, k, spec)
+    assert pr is not None and pr.shape == (1, Hq, w, L) and pr.dtype == torch.float32
+    o1, lse1 = esa.ops.forward(q, k, v, spec, scale, probs=pr)
+    o0, lse0 = esa.ops.forward(q, k, v, spec, scale)
+    assert torch.equal(o1, o0) and torch.equal(lse1, lse0)
+    idx, mask, _ = pattern.prepared_indices(Hq, w, layer, 8, L, L, L)
+    ti, tm = torch.from_numpy(idx).to(DEV), torch.from_numpy(mask).to(DEV)
+    _, w_ref = naive.naive_forward(q.float(), k.float(), v.float(), ti, tm, scale, G,
+                                   chunk=1024, return_weights=True)
+    err = (pr.permute(0, 1, 3, 2) - w_ref).abs().max().item()
+    assert err < 4e-3, err     # weights rounded to the input type once in the forward
+    g1 = esa.ops.backward(q, k, v, o1, lse1, do, spec, scale, probs=pr)
+    g0 = esa.ops.backward(q, k, v, o0, lse0, do, spec, scale)
+    ref = naive.naive_forward_backward_manual(q.float(), k.float(), v.float(), do.float(), ti, tm,
+                                              scale, G)
+    for a, b_, r_, t in zip(g1, g0, ref[1:], ("dq", "dk", "dv")):
+        assert_close(a, r_, dtype, f"saved probs {t}")
+        assert (a.float() - b_.float()).abs().max().item() < 2e-2
+    # no probabilities where the forward does not write them (layer 0: tensor cores)
+    if D == 128 and G in (2, 4, 8):
+        assert esa.ops.probs_buffer(q, k, esa.PatternSpec(0, 8, 64)) is None
