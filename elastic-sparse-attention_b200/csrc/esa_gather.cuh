@@ -202,6 +202,9 @@ constexpr int kTileMaxW = 64;
 constexpr int kTileIdxStride = kTileMaxW + 1;
 constexpr int kTileSpStride = kTileMaxW + 2;
 constexpr int kTileSidxBytes = kTilePairs * kTileIdxStride * 4;
+// sidx, fp32 scores (later the weights in the input type), per-pair 1 / sum.
+// Kept small: shared memory comes out of the same 256 KB per SM as the L1
+// that serves the shared K / V rows.
 constexpr int kTileSmemBytes = 2 * kTileSidxBytes + kTilePairs * 4;
 
 template <typename T, int D>
@@ -324,31 +327,25 @@ fwd_tile_kernel(const AttnParams p) {
       l += M::to_float(e);
     }
     l += __shfl_xor_sync(0xffffffffu, l, 1);
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const int j = j0 + pi / G;
+    const int h = hkv * G + pi % G;
     if ((threadIdx.x & 1) == 0) {
-      sl[pi] = l;
-      const int j = j0 + pi / G;
-      const int h = hkv * G + pi % G;
+      sl[pi] = inv;
       if (j < p.n_rows) p.lse[((int64_t)b * p.Hq + h) * p.n_rows + j] = mx + log2f(l);
+    }
+    // optional: the normalised probabilities for the backward, fp32 from the
+    // fp32 scores (what the backward would recompute from lse), slot-major
+    // [B, Hq, w, n]; the 4 bytes of neighbouring queries come from
+    // neighbouring warps and merge in L2
+    if (p.probs && j < p.n_rows) {
+      float* dst = p.probs + ((int64_t)(b * p.Hq + h) * w + kbeg) * p.n_rows + j;
+#pragma unroll
+      for (int i = 0; i < HALF; ++i)
+        if (kbeg + i < w) dst[(int64_t)i * p.n_rows] = exp2f(v[i] - mx) * inv;
     }
   }
   __syncthreads();
-
-  // ---- optional: the normalised probabilities for the backward, slot-major
-  // [B, Hq, w, n]; warp per (head, slot), lanes over consecutive queries so
-  // every store instruction writes whole 128-byte lines ----------------------
-  if (p.probs) {
-    for (int hk = warp; hk < G * w; hk += 8) {
-      const int hl = hk / w;
-      const int k = hk - hl * w;
-      float* dst = p.probs + (((int64_t)b * p.Hq + hkv * G + hl) * w + k) * p.n_rows + j0;
-      for (int jl = lane; jl < TQ; jl += 32) {
-        if (j0 + jl >= p.n_rows) break;
-        const int pi = jl * G + hl;
-        const float lm = sl[pi];
-        dst[jl] = lm > 0.f ? M::to_float(sp[pi][k]) / lm : 0.f;
-      }
-    }
-  }
 
   // ---- O = P V: lane keeps the EPL output dims r*EPL.. of its MI pairs ----
   float acc[MI][EPL];
@@ -372,8 +369,7 @@ fwd_tile_kernel(const AttnParams p) {
     const int j = j0 + pi / G;
     const int h = hkv * G + pi % G;
     if (j < p.n_rows) {
-      const float lm = sl[pi];
-      const float inv = lm > 0.f ? 1.f / lm : 0.f;
+      const float inv = sl[pi];
 #pragma unroll
       for (int e = 0; e < EPL; ++e) acc[m][e] *= inv;
       T* orow = reinterpret_cast<T*>(p.o) + b * p.sob + h * p.soh + (int64_t)j * p.sos + r * EPL;
@@ -466,13 +462,13 @@ bwd_query_tile_kernel(const AttnParams p) {
 
   // ---- pass 1a: p = exp2(s * scale_log2 - lse), or the forward's p --------
   if (p.probs) {
-    for (int hk = warp; hk < G * w; hk += 8) {
-      const int hl = hk / w;
-      const int k = hk - hl * w;
-      const float* src = p.probs + (((int64_t)b * p.Hq + hkv * G + hl) * w + k) * n + j0;
-      for (int jl = lane; jl < TQ; jl += 32) {
-        if (j0 + jl >= n) break;
-        sprob[jl * G + hl][k] = src[jl];
+    const int lg = __ffs(G) - 1;   // same lane order as the forward's write
+    for (int k = warp; k < w; k += 8) {
+      for (int pi = lane; pi < kTilePairs; pi += 32) {
+        const int j = j0 + (pi >> lg);
+        if (j >= n) break;
+        const int h = hkv * G + (pi & (G - 1));
+        sprob[pi][k] = p.probs[(((int64_t)b * p.Hq + h) * w + k) * n + j];
       }
     }
     __syncthreads();
