@@ -321,7 +321,9 @@ def bench_ours(args, world, rank, local):
         "per_layer": per_layer,
         "active_blocks_per_layer": [a for a, _ in blocks],
         "roofline": roofline,
-        "gpu_launches": args.steps * NL * (2 + HQ // HKV),
+        # per step: layer 0 = window forward + 2 window backward kernels; layers
+        # 1..7 = tile forward + query-side tile backward + G key-side launches
+        "gpu_launches": args.steps * (3 + (NL - 1) * (2 + HQ // HKV)),
         "clocks": clocks.summary(),
         "e2e": e2e,
     }

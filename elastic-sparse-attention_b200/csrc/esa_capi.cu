@@ -21,6 +21,7 @@
 #include "esa_layer.cuh"
 #include "esa_pattern.cuh"
 #include "esa_window_tc.cuh"
+#include "esa_window_bwd.cuh"
 
 namespace {
 
@@ -309,6 +310,41 @@ int launch_window(const esa::AttnParams& p, cudaStream_t s) {
   return check_launch("forward (tensor-core window)");
 }
 
+// Tensor-core backward of a sliding-window layer: dQ (query-major, also the
+// row values delta = rowsum(dO o O), kept in the workspace) then dK / dV
+// (key-major, all heads of a group in one CTA).
+template <typename T, int HT>
+int launch_window_bwd(const esa::AttnParams& p, cudaStream_t s) {
+  constexpr int QT = esa::kWinRows / HT;
+  const int nk = (QT + p.pat.w - 1 + 15) / 16 * 16;
+  const bool fp16 = std::is_same<T, __half>::value;
+  float* delta = reinterpret_cast<float*>(p.pds);   // [B, Hq, n_rows] in the workspace
+  esa::WindowBwdTmaps a, b;
+  if (!encode_map(&a.q, p.q, fp16, p.D, p.n_rows, p.Hq, p.B, p.sqs, p.sqh, p.sqb, QT) ||
+      !encode_map(&a.dout, p.dout, fp16, p.D, p.n_rows, p.Hq, p.B, p.sdos, p.sdoh, p.sdob, QT) ||
+      !encode_map(&a.k, p.k, fp16, p.D, p.kv_rows, p.Hkv, p.B, p.sks, p.skh, p.skb, nk) ||
+      !encode_map(&a.v, p.v, fp16, p.D, p.kv_rows, p.Hkv, p.B, p.svs, p.svh, p.svb, nk) ||
+      !encode_map(&b.q, p.q, fp16, p.D, p.n_rows, p.Hq, p.B, p.sqs, p.sqh, p.sqb, esa::kWbkQC) ||
+      !encode_map(&b.dout, p.dout, fp16, p.D, p.n_rows, p.Hq, p.B, p.sdos, p.sdoh, p.sdob,
+                  esa::kWbkQC) ||
+      !encode_map(&b.k, p.k, fp16, p.D, p.kv_rows, p.Hkv, p.B, p.sks, p.skh, p.skb, esa::kWbkKeys) ||
+      !encode_map(&b.v, p.v, fp16, p.D, p.kv_rows, p.Hkv, p.B, p.svs, p.svh, p.svb, esa::kWbkKeys))
+    return fail(ESA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the window backward");
+  auto kq = esa::window_bwd_dq_tc_kernel<T, HT>;
+  auto kkv = esa::window_bwd_dkv_tc_kernel<T>;
+  if (cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           esa::kWbqSmemBytes) != cudaSuccess ||
+      cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           esa::kWbkSmemBytes) != cudaSuccess)
+    return fail(ESA_ERR_CUDA, "cannot reserve shared memory for the window backward");
+  dim3 gq((p.n_rows + QT - 1) / QT, p.Hkv * (p.G / HT), p.B);
+  kq<<<gq, esa::kWinBwdThreads, esa::kWbqSmemBytes, s>>>(a, p, nk, delta);
+  if (int rc = check_launch("backward (tensor-core window, dQ)")) return rc;
+  dim3 gk((p.kv_rows + esa::kWbkKeys - 1) / esa::kWbkKeys, p.Hkv, p.B);
+  kkv<<<gk, esa::kWinBwdThreads, esa::kWbkSmemBytes, s>>>(b, p, delta);
+  return check_launch("backward (tensor-core window, dK dV)");
+}
+
 // Whether esa_forward for this call runs the tile kernel, the only one that
 // writes `probs` (and so whether the backward may read them).
 template <typename T, int D>
@@ -356,6 +392,14 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
   // probabilities from the forward only where that forward wrote them
   esa::AttnParams p = p_in;
   if (p.probs && !forward_writes_probs<T, D>(p)) p.probs = nullptr;
+  if constexpr (!std::is_same<T, float>::value && D == esa::kWinHeadDim) {
+    if (p.n_rows > 0 && !(p.flags & ESA_FLAG_GATHER_ONLY) && p.sdob > 0 && p.sdoh > 0 &&
+        p.sdos > 0) {
+      const int ht = window_heads<T, D>(p, p.alpha_zero, p.flags);
+      if (ht == 4) return launch_window_bwd<T, 4>(p, s);
+      if (ht == 2) return launch_window_bwd<T, 2>(p, s);
+    }
+  }
   bool query_done = false;
   if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
     if (p.n_rows > 0 && tile_path<T, D>(p)) {

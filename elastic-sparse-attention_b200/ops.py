@@ -158,11 +158,12 @@ def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
              rows: torch.Tensor | None = None, row_offset: int = 0, kv_len: int | None = None,
              kv_offset: int = 0, sorted_rows=None, row_perm=None, workspace=None,
              dropout_p: float = 0.0, dropout_seed: int = 0, dq=None, dk=None, dv=None,
-             probs: torch.Tensor | None = None):
+             probs: torch.Tensor | None = None, gather_only: bool = False):
     """Backward pass.  Returns (dq, dk, dv) in the input dtype.  With dropout,
     pass the forward's dropout_p and dropout_seed (the keep mask is rebuilt).
     dq / dk / dv may be given as (strided) views to write the gradients into,
-    e.g. the q / k / v parts of one fused QKV gradient buffer."""
+    e.g. the q / k / v parts of one fused QKV gradient buffer.  ``gather_only``
+    keeps sliding-window layers off the tensor-core backward (cross-checks)."""
     dev = _check_device(q, k, v, o, lse, dout)
     dq = torch.empty_like(q) if dq is None else dq
     dk = torch.empty_like(k) if dk is None else dk
@@ -173,7 +174,8 @@ def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
     if probs is not None:
         _check_probs(probs, q, spec)
     pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
-                  kv_offset, 0, dropout_p, dropout_seed, None, probs)
+                  kv_offset, _lib.FLAG_GATHER_ONLY if gather_only else 0, dropout_p,
+                  dropout_seed, None, probs)
     lib = _lib.load()
     need = lib.esa_backward_workspace_size(ctypes.byref(pb))
     if workspace is None or workspace.numel() < need:

@@ -474,3 +474,33 @@ def test_saved_probs_forward_backward(esa, dtype, G, w, D, L, layer):
     # no probabilities where the forward does not write them (layer 0: tensor cores)
     if D == 128 and G in (2, 4, 8):
         assert esa.ops.probs_buffer(q, k, esa.PatternSpec(0, 8, 64)) is None
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("G,w,L,q_len", [(4, 64, 1000, 1000), (4, 97, 333, 333), (8, 64, 517, 517),
+                                         (2, 64, 700, 700), (2, 65, 130, 130), (4, 64, 50, 50),
+                                         (4, 16, 600, 300), (12, 40, 257, 257), (4, 64, 4099, 4099)])
+def test_window_tensor_core_backward(esa, dtype, G, w, L, q_len):
+    """Layer 0 backward on the tcgen05 kernels (dQ query-major, dK/dV
+    key-major over all heads of a group): against the CUDA-core backward and
+    the fp32 oracle, including ragged tiles, prefill (q_len < kv_len), GQA
+    group sizes 2..12 and windows longer than the sequence."""
+    g = torch.Generator().manual_seed(G * 77 + w + L)
+    Hkv, D = 2, 128
+    Hq = Hkv * G
+    q, do = randn(1, Hq, q_len, D, dtype=dtype, gen=g), randn(1, Hq, q_len, D, dtype=dtype, gen=g)
+    k, v = randn(1, Hkv, L, D, dtype=dtype, gen=g), randn(1, Hkv, L, D, dtype=dtype, gen=g)
+    spec = esa.PatternSpec(0, 8, w)
+    o, lse = esa.ops.forward(q, k, v, spec, D ** -0.5)
+    esa.ops.device_errors()
+    g_tc = esa.ops.backward(q, k, v, o, lse, do, spec, D ** -0.5)
+    assert esa.ops.device_errors() == 0
+    g_ga = esa.ops.backward(q, k, v, o, lse, do, spec, D ** -0.5, gather_only=True)
+    idx, mask, _ = pattern.prepared_indices(Hq, w, 0, 8, L, q_len, L)
+    ref = naive.naive_forward_backward_manual(q.float(), k.float(), v.float(), do.float(),
+                                              torch.from_numpy(idx).to(DEV),
+                                              torch.from_numpy(mask).to(DEV), D ** -0.5, G)
+    for a, b_, r_, t in zip(g_tc, g_ga, ref[1:], ("dq", "dk", "dv")):
+        assert_close(a, r_, dtype, f"window bwd G{G} w{w} L{L} {t}")
+        # the two paths round differently: within one output ulp of each other
+        assert ((a.float() - b_.float()).abs() - 2 * HALF_ULP[dtype] * b_.float().abs()).max().item() < 2e-2, t
