@@ -424,7 +424,7 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
   }
   {
     const int ncol = (p.pat.w + 31) >> 5;
-    const size_t smem = (size_t)kKeyWarps * (esa::KeyStage<T, D>::kWarpBytes + ncol * 32 * sizeof(int));
+    const size_t smem = (size_t)kKeyWarps * (esa::KeyStage<T, D>::kWarpBytes + ncol * 64 * sizeof(int));
     auto kern = esa::bwd_key_kernel<T, D, kKeyWarps, kKeyRowsPerWarp>;
     if (int rc = prepare_smem(kern, smem)) return rc;
     const int tile = kKeyWarps * kKeyRowsPerWarp;

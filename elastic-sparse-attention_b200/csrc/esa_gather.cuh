@@ -727,7 +727,11 @@ bwd_key_kernel(const AttnParams p) {
   const int ncol = (w + 31) >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned char* ring = smem_raw + warp * S::kWarpBytes;
-  int* scur = reinterpret_cast<int*>(smem_raw + NW * S::kWarpBytes) + warp * ncol * 32;
+  // per column: cursor (first query slot not yet assigned to a key) and the
+  // key index at the cursor (so a column with no user for a key costs no
+  // index computation)
+  int* scur = reinterpret_cast<int*>(smem_raw + NW * S::kWarpBytes) + warp * ncol * 64;
+  int* sval = scur + ncol * 32;
   const int g = lane / LPR, r = lane % LPR;
   const int hkv = blockIdx.y, b = blockIdx.z;
   const int h = hkv * p.G + p.head_in_group;
@@ -759,6 +763,7 @@ bwd_key_kernel(const AttnParams p) {
         lo = a;
       }
       scur[cc * 32 + lane] = lo;
+      sval[cc * 32 + lane] = (k < w && lo < n) ? cidx(lo, k) : 0x7fffffff;
     }
   }
 
@@ -780,17 +785,25 @@ bwd_key_kernel(const AttnParams p) {
       const int k = lane + 32 * cc;
       const int start = scur[cc * 32 + lane];
       int len = 0;
-      if (k < w && start < n && cidx(start, k) == P) {
-        // Gallop to the end of the run of query slots that use key P.
-        int lo = start, step = 1;
-        while (lo + step < n && cidx(lo + step, k) == P) { lo += step; step <<= 1; }
+      if (sval[cc * 32 + lane] == P) {   // the column's next users are key P's
+        // Gallop to the end of the run of query slots that use key P; hv is
+        // the key at hi once known (hi = n: none).
+        int lo = start, step = 1, hv = 0x7fffffff;
+        while (lo + step < n) {
+          const int c = cidx(lo + step, k);
+          if (c != P) { hv = c; break; }
+          lo += step;
+          step <<= 1;
+        }
         int hi = min(lo + step, n);
         while (hi - lo > 1) {
           const int mid = (lo + hi) >> 1;
-          if (cidx(mid, k) == P) lo = mid; else hi = mid;
+          const int c = cidx(mid, k);
+          if (c == P) lo = mid; else { hi = mid; hv = c; }
         }
         len = hi - start;
         scur[cc * 32 + lane] = hi;
+        sval[cc * 32 + lane] = hi < n ? hv : 0x7fffffff;
       }
       // Flatten the lanes' runs: exclusive prefix of run lengths.
       int off = len;
