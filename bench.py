@@ -322,8 +322,9 @@ def bench_ours(args, world, rank, local):
         "active_blocks_per_layer": [a for a, _ in blocks],
         "roofline": roofline,
         # per step: layer 0 = window forward + 2 window backward kernels; layers
-        # 1..7 = tile forward + query-side tile backward + G key-side launches
-        "gpu_launches": args.steps * (3 + (NL - 1) * (2 + HQ // HKV)),
+        # 1..7 = tile forward + query-side tile backward + long-run chunk kernel
+        # + G key-side launches
+        "gpu_launches": args.steps * (3 + (NL - 1) * (3 + HQ // HKV)),
         "clocks": clocks.summary(),
         "e2e": e2e,
     }
@@ -399,7 +400,7 @@ def e2e_module(esa, args, dev, world):
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    n = max(3, args.steps)
+    n = max(10, args.steps)   # enough steps that the pipeline's fill and drain amortise
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(compute)
     h2d_stream.wait_event(e0)

@@ -422,6 +422,11 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
     kern<<<grid, kFwdWarps * 32, smem, s>>>(p, rpc);
     if (int rc = check_launch("backward (query side)")) return rc;
   }
+  if (p.heavy_chunks > 0) {
+    // partial sums of query chunks that all use one key (long runs)
+    esa::bwd_heavy_kernel<T, D><<<dim3(p.heavy_chunks, p.Hq, p.B), 256, 0, s>>>(p);
+    if (int rc = check_launch("backward (key side, long runs)")) return rc;
+  }
   {
     const int ncol = (p.pat.w + 31) >> 5;
     const size_t smem = (size_t)kKeyWarps * (esa::KeyStage<T, D>::kWarpBytes + ncol * 64 * sizeof(int));
@@ -497,6 +502,12 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 size_t pds_bytes(const esa_problem_t* pb) {
   return align256((size_t)pb->batch * pb->num_heads * pb->attn_length * pb->q_len * sizeof(float2));
 }
+size_t heavy_bytes(const esa_problem_t* pb) {
+  const int64_t chunks = pb->q_len / esa::kHeavyChunk;
+  return align256((size_t)pb->batch * pb->num_heads * pb->attn_length * chunks * 2 *
+                  pb->head_dim * sizeof(float));
+}
+
 size_t acc_bytes(const esa_problem_t* pb) {
   if (pb->num_heads == pb->num_kv_heads) return 0;
   return align256((size_t)2 * pb->batch * pb->num_kv_heads * pb->kv_rows * pb->head_dim *
@@ -590,7 +601,7 @@ int esa_forward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_ten
 
 size_t esa_backward_workspace_size(const esa_problem_t* pb) {
   if (!pb || pb->batch < 0 || pb->q_len < 0 || pb->attn_length < 0) return 0;
-  return pds_bytes(pb) + acc_bytes(pb);
+  return pds_bytes(pb) + acc_bytes(pb) + heavy_bytes(pb);
 }
 
 int esa_backward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_tensor_t v,
@@ -636,6 +647,8 @@ int esa_backward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_te
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   p.pds = reinterpret_cast<float2*>(ws);
   p.acc = acc_bytes(pb) ? reinterpret_cast<float*>(ws + pds_bytes(pb)) : nullptr;
+  p.heavy_chunks = (int)(pb->q_len / esa::kHeavyChunk);
+  p.heavy = p.heavy_chunks ? reinterpret_cast<float*>(ws + pds_bytes(pb) + acc_bytes(pb)) : nullptr;
   return dispatch_op<BwdOp>(pb->dtype, pb->head_dim, p, (cudaStream_t)stream);
 }
 

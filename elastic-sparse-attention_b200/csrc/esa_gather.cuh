@@ -681,6 +681,87 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
 }
 
 // ---------------------------------------------------------------------------
+// Backward, key side, long runs: for every chunk of kHeavyChunk consecutive
+// query slots whose users all use one key in a (head, slot) column (with the
+// per-slot index monotone in position, the first and the last slot decide),
+// the sums of dS*scale q and p dO over the chunk, into
+// heavy[b, h, slot, chunk, {dK, dV}, D] (fp32).  bwd_key_kernel skips those
+// chunks and adds the partials, so a key that receives a whole column's
+// queries (alpha = 1, head 0, slot 0: every query uses key 0) is summed by
+// many warps instead of one.  grid = (n_rows / kHeavyChunk, Hq, B).
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(256)
+bwd_heavy_kernel(const AttnParams p) {
+  using L = Layout<T, D>;
+  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  constexpr int UNROLL = 4;
+  static_assert(kHeavyChunk % (RPW * UNROLL) == 0, "chunk must split into whole steps");
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane / LPR, r = lane % LPR;
+  const int n = p.n_rows, w = p.pat.w;
+  const int j0 = c * kHeavyChunk;
+  const float t = head_weight(p.pat, h);
+  const float omt = __fsub_rn(1.f, t);
+  const int64_t* srows = p.sorted_rows ? p.sorted_rows : p.rows;
+  const int kvmax = p.kv_len - 1;
+  auto cidx = [&](int jq, int k) -> int {
+    const int pos = srows ? (int)srows[jq] : p.row_offset + jq;
+    return min(raw_index(row_window(p.pat, pos), k, t, omt), kvmax);
+  };
+  const float2* pdsb = p.pds + (int64_t)(b * p.Hq + h) * w * n;
+  const T* qb = reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh + r * EPL;
+  const T* db = reinterpret_cast<const T*>(p.dout) + b * p.sdob + h * p.sdoh + r * EPL;
+  for (int k = warp; k < w; k += blockDim.x >> 5) {
+    int constant = 0;
+    if (lane == 0) constant = cidx(j0, k) == cidx(j0 + kHeavyChunk - 1, k);
+    if (!__shfl_sync(0xffffffffu, constant, 0)) continue;
+    float adk[EPL], adv[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) { adk[e] = 0.f; adv[e] = 0.f; }
+    const float2* pk = pdsb + (int64_t)k * n;
+    for (int u = g; u < kHeavyChunk; u += RPW * UNROLL) {
+      int qi[UNROLL];
+      float2 pd[UNROLL];
+      uint4 qv[UNROLL], dv[UNROLL];
+#pragma unroll
+      for (int x = 0; x < UNROLL; ++x) {
+        const int jq = j0 + u + x * RPW;
+        qi[x] = p.row_perm ? (int)p.row_perm[jq] : jq;
+      }
+#pragma unroll
+      for (int x = 0; x < UNROLL; ++x) {
+        pd[x] = pk[qi[x]];
+        qv[x] = ldg16_stream(qb + (int64_t)qi[x] * p.sqs);
+        dv[x] = ldg16_stream(db + (int64_t)qi[x] * p.sdos);
+      }
+#pragma unroll
+      for (int x = 0; x < UNROLL; ++x) {
+        axpy_f32<T>(pd[x].y, qv[x], adk);
+        axpy_f32<T>(pd[x].x, dv[x], adv);
+      }
+    }
+#pragma unroll
+    for (int o = LPR; o < 32; o <<= 1)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        adk[e] += __shfl_xor_sync(0xffffffffu, adk[e], o);
+        adv[e] += __shfl_xor_sync(0xffffffffu, adv[e], o);
+      }
+    if (g == 0) {
+      float* part = p.heavy + ((((int64_t)b * p.Hq + h) * w + k) * p.heavy_chunks + c) * (2 * D) +
+                    r * EPL;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        part[e] = adk[e];
+        part[D + e] = adv[e];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Backward, key side, for query head (hkv * G + head_in_group) of every group.
 // grid = (ceil(kv_rows / (NW * RW)), Hkv, B); warp owns RW consecutive key
 // rows; lanes own slot columns k = lane + 32 * cc.  With G > 1 the G launches
@@ -775,36 +856,11 @@ bwd_key_kernel(const AttnParams p) {
   const int64_t drow_bytes = p.sdos * (int64_t)sizeof(T);
   const float2* pdsb = p.pds + (int64_t)(b * p.Hq + h) * w * n;
 
-  for (int lr = lr0; lr < lr1; ++lr) {
-    const int P = p.kv_offset + lr;
-    float adk[EPL], adv[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) { adk[e] = 0.f; adv[e] = 0.f; }
-
-    for (int cc = 0; cc < ncol; ++cc) {
-      const int k = lane + 32 * cc;
-      const int start = scur[cc * 32 + lane];
-      int len = 0;
-      if (sval[cc * 32 + lane] == P) {   // the column's next users are key P's
-        // Gallop to the end of the run of query slots that use key P; hv is
-        // the key at hi once known (hi = n: none).
-        int lo = start, step = 1, hv = 0x7fffffff;
-        while (lo + step < n) {
-          const int c = cidx(lo + step, k);
-          if (c != P) { hv = c; break; }
-          lo += step;
-          step <<= 1;
-        }
-        int hi = min(lo + step, n);
-        while (hi - lo > 1) {
-          const int mid = (lo + hi) >> 1;
-          const int c = cidx(mid, k);
-          if (c == P) lo = mid; else { hi = mid; hv = c; }
-        }
-        len = hi - start;
-        scur[cc * 32 + lane] = hi;
-        sval[cc * 32 + lane] = hi < n ? hv : 0x7fffffff;
-      }
+  float adk[EPL], adv[EPL];
+  // Streams the users of the lanes' runs [start, start + len) of column chunk
+  // cc: flattened over lanes, moved with cp.async into two shared-memory
+  // stages of UB users, accumulated into adk / adv.
+  auto stream_runs = [&](const int start, const int len, const int cc) {
       // Flatten the lanes' runs: exclusive prefix of run lengths.
       int off = len;
 #pragma unroll
@@ -814,8 +870,7 @@ bwd_key_kernel(const AttnParams p) {
       }
       const int total = __shfl_sync(0xffffffffu, off, 31);
       off -= len;
-      if (total == 0) continue;
-
+      if (total == 0) return;
       // Resolve users u0 + lane (lane < UB) and start their row copies into
       // stage `st`; returns this lane's (p, dS) of its user (0 when none).
       // They stay fp32: a key row can have ~1e5 users (alpha = 1, head 0,
@@ -880,7 +935,75 @@ bwd_key_kernel(const AttnParams p) {
         s_cur = s_nxt;
         st ^= 1;
       }
+  };
+  for (int lr = lr0; lr < lr1; ++lr) {
+    const int P = p.kv_offset + lr;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) { adk[e] = 0.f; adv[e] = 0.f; }
+
+    for (int cc = 0; cc < ncol; ++cc) {
+      const int k = lane + 32 * cc;
+      const int start = scur[cc * 32 + lane];
+      int len = 0;
+      if (sval[cc * 32 + lane] == P) {   // the column's next users are key P's
+        // Gallop to the end of the run of query slots that use key P; hv is
+        // the key at hi once known (hi = n: none).
+        int lo = start, step = 1, hv = 0x7fffffff;
+        while (lo + step < n) {
+          const int c = cidx(lo + step, k);
+          if (c != P) { hv = c; break; }
+          lo += step;
+          step <<= 1;
+        }
+        int hi = min(lo + step, n);
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          const int c = cidx(mid, k);
+          if (c == P) lo = mid; else { hi = mid; hv = c; }
+        }
+        len = hi - start;
+        scur[cc * 32 + lane] = hi;
+        sval[cc * 32 + lane] = hi < n ? hv : 0x7fffffff;
+      }
+      // Full kHeavyChunk-aligned chunks inside a long run were summed by
+      // bwd_heavy_kernel; stream only the pieces before and after them.
+      int hc0 = 0, hc1 = 0, start2 = 0, len2 = 0, len1 = len;
+      if (p.heavy_chunks > 0 && len >= kHeavyChunk) {
+        const int e = start + len;
+        const int c0 = (start + kHeavyChunk - 1) / kHeavyChunk;
+        const int c1 = min(e / kHeavyChunk, p.heavy_chunks);
+        if (c1 > c0) {
+          hc0 = c0;
+          hc1 = c1;
+          len1 = c0 * kHeavyChunk - start;
+          start2 = c1 * kHeavyChunk;
+          len2 = e - start2;
+        }
+      }
+      stream_runs(start, len1, cc);
+      if (__any_sync(0xffffffffu, len2 > 0)) stream_runs(start2, len2, cc);
+      // add the chunk partials (each lane of row group 0 its D slice)
+      unsigned hm = __ballot_sync(0xffffffffu, hc1 > hc0);
+      while (hm) {
+        const int src = __ffs(hm) - 1;
+        hm &= hm - 1;
+        const int ck = __shfl_sync(0xffffffffu, k, src);
+        const int a = __shfl_sync(0xffffffffu, hc0, src);
+        const int z = __shfl_sync(0xffffffffu, hc1, src);
+        if (g == 0) {
+          const float* part = p.heavy + ((((int64_t)b * p.Hq + h) * w + ck) * p.heavy_chunks + a) *
+                                            (2 * D) + r * EPL;
+          for (int c = a; c < z; ++c, part += 2 * D) {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+              adk[e] += part[e];
+              adv[e] += part[D + e];
+            }
+          }
+        }
+      }
     }
+
 #pragma unroll
     for (int o = LPR; o < 32; o <<= 1)
 #pragma unroll

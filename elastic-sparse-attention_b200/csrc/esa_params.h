@@ -46,7 +46,14 @@ struct AttnParams {
   uint64_t seed;
   void* weights;               // optional [B, Hq, n_rows, w] weights output (input dtype)
   float* probs;                // optional fp32 [B, Hq, w, n_rows] probabilities (tile path)
+  // Key side: partial dK / dV sums of "constant" query chunks (kHeavyChunk
+  // consecutive query slots that all use one key in a (head, slot) column),
+  // fp32 [B, Hq, w, heavy_chunks, 2, D]; heavy_chunks = n_rows / kHeavyChunk.
+  float* heavy;
+  int heavy_chunks;
 };
+
+constexpr int kHeavyChunk = 1024;
 
 __device__ __forceinline__ bool dropout_keep(const AttnParams& p, int pos, int bh, int k) {
   const uint4 r = philox4x32_10(make_uint4((uint32_t)pos, (uint32_t)bh, (uint32_t)(k >> 2), 0u),

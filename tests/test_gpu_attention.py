@@ -504,3 +504,23 @@ def test_window_tensor_core_backward(esa, dtype, G, w, L, q_len):
         assert_close(a, r_, dtype, f"window bwd G{G} w{w} L{L} {t}")
         # the two paths round differently: within one output ulp of each other
         assert ((a.float() - b_.float()).abs() - 2 * HALF_ULP[dtype] * b_.float().abs()).max().item() < 2e-2, t
+
+
+@pytest.mark.parametrize("dtype,G,L,perm", [(torch.bfloat16, 4, 5000, False), (torch.float32, 2, 4100, False),
+                                            (torch.float32, 4, 3000, True)])
+def test_long_runs_split_into_chunks(esa, dtype, G, L, perm):
+    """alpha = 1 (last layer): head 0's slot 0 sends every query to key 0, and
+    other heads' slot 0 has runs of thousands of queries.  Full 1024-slot
+    chunks of such runs are summed by the chunk kernel and added by the key
+    side; gradients must match the oracle, also with unsorted query rows
+    (cache_position, sorted on the host with a permutation)."""
+    g = torch.Generator().manual_seed(L + G)
+    Hkv, D, nl = 2, 64, 8
+    Hq = Hkv * G
+    q, do = randn(1, Hq, L, D, dtype=dtype, gen=g), randn(1, Hq, L, D, dtype=dtype, gen=g)
+    k, v = randn(1, Hkv, L, D, dtype=dtype, gen=g), randn(1, Hkv, L, D, dtype=dtype, gen=g)
+    cp = torch.randperm(L, generator=g).to(DEV) if perm else None
+    o, dq, dk, dv = run_module(esa, q, k, v, do, nl - 1, nl, 64, cache_position=cp)
+    ref = run_oracle(q, k, v, do, nl - 1, nl, 64, cache_position=cp)
+    for got, want, t in zip((o, dq, dk, dv), ref, ("out", "dq", "dk", "dv")):
+        assert_close(got, want, dtype, f"long runs {dtype} G{G} L{L} {t}")
