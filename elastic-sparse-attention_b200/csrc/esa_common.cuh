@@ -12,6 +12,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <type_traits>
 
 namespace esa {
 
@@ -233,10 +234,31 @@ __device__ __forceinline__ void ffma2(float& c0, float& c1, float a0, float a1, 
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
+// Low bf16 half of a 32-bit word to fp32 on the FMA pipe: lo * 1 + (-0) is
+// exact (and keeps the sign of zero), so half of a vector's conversions leave
+// the integer pipe, which the shift / mask forms of the other half use.
+__device__ __forceinline__ float bf16_lo_to_f32_fma(uint32_t u) {
+  float f;
+  asm("{\n\t.reg .b16 l, h, one;\n\t"
+      "mov.b32 {l, h}, %1;\n\tmov.b16 one, 0x3F80;\n\t"
+      "fma.rn.f32.bf16 %0, l, one, %2;\n\t}"
+      : "=f"(f)
+      : "r"(u), "f"(-0.0f));
+  return f;
+}
+
 template <typename T>
 __device__ __forceinline__ void axpy_f32(float s, const uint4& b, float* acc) {
   if constexpr (sizeof(T) == 4) {
     Mix<float>::axpy(s, b, acc);
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float lo = bf16_lo_to_f32_fma(w[i]);
+      const float hi = __uint_as_float(w[i] & 0xffff0000u);
+      ffma2(acc[2 * i], acc[2 * i + 1], s, s, lo, hi);
+    }
   } else {
     float f[8];
     Vec<T>::to_float(b, f);
