@@ -283,7 +283,7 @@ bool tile_path(const esa::AttnParams& p) {
     return false;
   } else {
     return p.pat.w <= esa::kTileMaxW && p.G <= esa::kTilePairs && esa::kTilePairs % p.G == 0 &&
-           !p.rows && p.n_rows >= 256 && !needs_gather(p);
+           !p.rows && p.n_rows >= 256 && p.kv_rows >= 1 && !needs_gather(p);
   }
 }
 

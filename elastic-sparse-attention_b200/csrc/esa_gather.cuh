@@ -181,6 +181,45 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
   }
 }
 
+// Rows of slots [kbeg, kbeg + half) of the pair (row j, head h) for the tile
+// kernels: the k/v buffer row of a valid slot; for a masked slot (and every
+// slot of a padding row j >= n_rows) the pair's slot-0 row, or row 0 when that
+// is masked too, with the sign bit set.  The tile kernels then load every
+// slot unconditionally from `row & kRowMask` (always inside the buffer) and
+// take the sign bit as the mask; a masked slot's weight is 0, and its row is
+// one the pair reads anyway, so no value it could not see enters the sums.
+constexpr int kMaskBit = int(0x80000000u);
+constexpr int kRowMask = 0x7fffffff;
+
+__device__ __forceinline__ void tile_slot_rows(const AttnParams& p, int j, int h, int kbeg,
+                                               int half, int* out) {
+  if (j >= p.n_rows) {
+    for (int k = kbeg; k < kbeg + half; ++k) out[k] = kMaskBit;
+    return;
+  }
+  const int w = p.pat.w;
+  const int pos = query_pos(p, j);
+  const RowWin rw = row_window(p.pat, pos);
+  const float t = head_weight(p.pat, h);
+  const float omt = __fsub_rn(1.f, t);
+  auto row_of = [&](int k) -> int {   // -1 when masked or outside the buffer
+    const int raw = raw_index(rw, k, t, omt);
+    if (pos < 0 || raw > pos) return -1;   // causal mask (:532)
+    const int row = min(raw, p.kv_len - 1) - p.kv_offset;   // clamp (:615)
+    if (row < 0 || row >= p.kv_rows) {
+      if (p.err) atomicOr(p.err, kErrKvRange);
+      return -1;
+    }
+    return row;
+  };
+  const int r0 = row_of(0);
+  const int fallback = kMaskBit | (r0 >= 0 ? r0 : 0);
+  for (int k = kbeg; k < kbeg + half; ++k) {
+    const int row = k < w ? (k == 0 ? r0 : row_of(k)) : -1;
+    out[k] = row >= 0 ? row : fallback;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Forward, slot-major tile variant (16-bit types, w <= 64, G divides 128).
 //
@@ -241,28 +280,7 @@ fwd_tile_kernel(const AttnParams p) {
     const int j = j0 + pi / G;
     const int h = hkv * G + pi % G;
     const int kbeg = (threadIdx.x & 1) * HALF;
-    if (j < p.n_rows) {
-      const int pos = query_pos(p, j);
-      const RowWin rw = row_window(p.pat, pos);
-      const float t = head_weight(p.pat, h);
-      const float omt = __fsub_rn(1.f, t);
-      for (int k = kbeg; k < kbeg + HALF; ++k) {
-        int row = -1;
-        if (k < w) {
-          const int raw = raw_index(rw, k, t, omt);
-          if (raw <= pos) {
-            row = min(raw, p.kv_len - 1) - p.kv_offset;
-            if (row < 0 || row >= p.kv_rows) {
-              if (p.err) atomicOr(p.err, kErrKvRange);
-              row = -1;
-            }
-          }
-        }
-        sidx[pi][k] = row;
-      }
-    } else {
-      for (int k = kbeg; k < kbeg + HALF; ++k) sidx[pi][k] = -1;
-    }
+    tile_slot_rows(p, j, h, kbeg, HALF, &sidx[pi][0]);
   }
   __syncthreads();
 
@@ -293,7 +311,7 @@ fwd_tile_kernel(const AttnParams p) {
 #pragma unroll
         for (int m = 0; m < MI; ++m) {
           const int row = sidx[pw0 + m * RPW + g][k0 + s2];
-          kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
+          kb[m] = ldg16(Kb + (int64_t)(row & kRowMask) * p.sks);
         }
 #pragma unroll
         for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(qv[m], kb[m], 0.f);
@@ -358,7 +376,7 @@ fwd_tile_kernel(const AttnParams p) {
 #pragma unroll
     for (int m = 0; m < MI; ++m) {
       const int row = sidx[pw0 + m * RPW + g][k];
-      vb[m] = row >= 0 ? ldg16(Vb + (int64_t)row * p.svs) : make_uint4(0, 0, 0, 0);
+      vb[m] = ldg16(Vb + (int64_t)(row & kRowMask) * p.svs);
     }
 #pragma unroll
     for (int m = 0; m < MI; ++m) M::axpy(sp[pw0 + m * RPW + g][k], vb[m], acc[m]);
@@ -419,28 +437,7 @@ bwd_query_tile_kernel(const AttnParams p) {
     const int j = j0 + pi / G;
     const int h = hkv * G + pi % G;
     const int kbeg = (threadIdx.x & 1) * HALF;
-    if (j < n) {
-      const int pos = query_pos(p, j);
-      const RowWin rw = row_window(p.pat, pos);
-      const float t = head_weight(p.pat, h);
-      const float omt = __fsub_rn(1.f, t);
-      for (int k = kbeg; k < kbeg + HALF; ++k) {
-        int row = -1;
-        if (k < w) {
-          const int raw = raw_index(rw, k, t, omt);
-          if (raw <= pos) {
-            row = min(raw, p.kv_len - 1) - p.kv_offset;
-            if (row < 0 || row >= p.kv_rows) {
-              if (p.err) atomicOr(p.err, kErrKvRange);
-              row = -1;
-            }
-          }
-        }
-        sidx[pi][k] = row;
-      }
-    } else {
-      for (int k = kbeg; k < kbeg + HALF; ++k) sidx[pi][k] = -1;
-    }
+    tile_slot_rows(p, j, h, kbeg, HALF, &sidx[pi][0]);
   }
   __syncthreads();
 
@@ -485,7 +482,7 @@ bwd_query_tile_kernel(const AttnParams p) {
 #pragma unroll
         for (int m = 0; m < MI; ++m) {
           const int row = sidx[pw0 + m * RPW + g][k0 + s2];
-          kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
+          kb[m] = ldg16(Kb + (int64_t)(row & kRowMask) * p.sks);
         }
 #pragma unroll
         for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(qv[m], kb[m], 0.f);
@@ -518,7 +515,7 @@ bwd_query_tile_kernel(const AttnParams p) {
 #pragma unroll
         for (int m = 0; m < MI; ++m) {
           const int row = sidx[pw0 + m * RPW + g][k0 + s2];
-          vb[m] = row >= 0 ? ldg16(Vb + (int64_t)row * p.svs) : make_uint4(0, 0, 0, 0);
+          vb[m] = ldg16(Vb + (int64_t)(row & kRowMask) * p.svs);
         }
 #pragma unroll
         for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(dv[m], vb[m], 0.f);
@@ -544,7 +541,7 @@ bwd_query_tile_kernel(const AttnParams p) {
 #pragma unroll
     for (int m = 0; m < MI; ++m) {
       const int row = sidx[pw0 + m * RPW + g][k];
-      kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
+      kb[m] = ldg16(Kb + (int64_t)(row & kRowMask) * p.sks);
     }
 #pragma unroll
     for (int m = 0; m < MI; ++m) M::axpy(sds[pw0 + m * RPW + g][k], kb[m], acc[m]);
