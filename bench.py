@@ -500,7 +500,8 @@ def bench_c5(args, world, rank, local):
             "config": {"workload": "C5: fwd+bwd of the 8 P8 layers, B=1, 16 heads, L=2^20, D=128, "
                                    "query rows split over the ranks, remote K/V fetched with NCCL",
                        "seq_len": L5, "rows_per_rank": S, "parallelism": f"sequence split x{world}",
-                       "max_rows_fetched_per_layer_per_rank": fetched},
+                       "max_rows_fetched_per_layer_per_rank": fetched,
+                       "allocator": os.environ.get("PYTORCH_CUDA_ALLOC_CONF", "default")},
             "clocks": clocks.summary()}
 
 
@@ -701,6 +702,10 @@ def main():
     if args.workload == "c4":
         print(json.dumps(bench_c4(args)), flush=True)
         return
+    if args.workload == "c5":
+        # every layer's K/V buffer has a different row count; expandable
+        # segments keep the cached blocks from fragmenting the 180 GB
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     world, rank, local = dist_init()
     if args.workload == "c5":
         line = bench_c5(args, world, rank, local)

@@ -18,6 +18,7 @@
 #include "esa_layer.h"
 #include "esa_decode.cuh"
 #include "esa_gather.cuh"
+#include "esa_keymma.cuh"
 #include "esa_layer.cuh"
 #include "esa_pattern.cuh"
 #include "esa_window_tc.cuh"
@@ -287,6 +288,30 @@ bool tile_path(const esa::AttnParams& p) {
   }
 }
 
+// The tensor-core key side: 16-bit types, D = 64 / 128, contiguous query
+// positions (no explicit rows), all G heads' columns in one warp's cursors.
+template <typename T, int D>
+bool key_mma_path(const esa::AttnParams& p) {
+  if constexpr (std::is_same<T, float>::value || !(D == 64 || D == 128)) {
+    return false;
+  } else {
+    using KM = esa::KeyMma<T, D>;
+    constexpr int64_t per16 = 16 / sizeof(T);
+    // q / dO rows are copied in 16-byte units addressed by 32-bit offsets
+    auto rows_ok = [&](const void* base, int64_t srow, int64_t shead, int64_t sbatch) {
+      if (reinterpret_cast<uintptr_t>(base) % 16 || srow % per16 || shead % per16 ||
+          sbatch % per16 || srow < 0 || shead < 0)
+        return false;
+      const int64_t last = (int64_t)(p.G - 1) * shead + (int64_t)(p.n_rows - 1) * srow;
+      return last / per16 < (int64_t(1) << 32);
+    };
+    return !p.rows && !p.sorted_rows && !p.row_perm && p.G <= KM::kMaxGroup &&
+           p.G * p.pat.w <= KM::kMaxCols && p.kv_rows >= 1 && p.n_rows >= 1 &&
+           !(p.flags & ESA_FLAG_GATHER_ONLY) && rows_ok(p.q, p.sqs, p.sqh, p.sqb) &&
+           rows_ok(p.dout, p.sdos, p.sdoh, p.sdob);
+  }
+}
+
 bool decode_path(const esa::AttnParams& p) {
   return (int64_t)p.B * p.Hq * p.n_rows <= kDecodeMaxPairs && !needs_gather(p);
 }
@@ -426,6 +451,18 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
     // partial sums of query chunks that all use one key (long runs)
     esa::bwd_heavy_kernel<T, D><<<dim3(p.heavy_chunks, p.Hq, p.B), 256, 0, s>>>(p);
     if (int rc = check_launch("backward (key side, long runs)")) return rc;
+  }
+  if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
+    if (key_mma_path<T, D>(p)) {
+      using KM = esa::KeyMma<T, D>;
+      const size_t smem = KM::smem_bytes(p.G * p.pat.w);
+      auto kern = esa::bwd_key_mma_kernel<T, D>;
+      if (int rc = prepare_smem(kern, smem)) return rc;
+      const int tile = KM::kWarps * KM::kTiles * KM::kKeys;
+      dim3 grid((p.kv_rows + tile - 1) / tile, p.Hkv, p.B);
+      kern<<<grid, KM::kWarps * 32, smem, s>>>(p);
+      return check_launch("backward (key side, tensor cores)");
+    }
   }
   {
     const int ncol = (p.pat.w + 31) >> 5;

@@ -146,8 +146,13 @@ class _ShardedFunction(torch.autograd.Function):
         qv = q.transpose(1, 2)                       # [B, Hq, S, D] view
         kv_k = kbuf.permute(1, 2, 0, 3)              # [B, Hkv, rows, D] view
         kv_v = vbuf.permute(1, 2, 0, 3)
-        o, lse = ops.forward(qv, kv_k, kv_v, spec, scale, row_offset=a0, kv_len=L, kv_offset=lo)
-        ctx.save_for_backward(q, kbuf, vbuf, o, lse)
+        probs = None
+        if hasattr(ops, "probs_buffer"):
+            # the forward leaves its probabilities for the backward (no score pass)
+            probs = ops.probs_buffer(qv, kv_k, spec, row_offset=a0, kv_len=L, kv_offset=lo)
+        o, lse = ops.forward(qv, kv_k, kv_v, spec, scale, row_offset=a0, kv_len=L, kv_offset=lo,
+                             **({"probs": probs} if probs is not None else {}))
+        ctx.save_for_backward(q, kbuf, vbuf, o, lse, probs)
         ctx.meta = (spec, scale, plan, rank, group, ops)
         return o.transpose(1, 2)                     # [B, S, Hq, D]
 
@@ -155,14 +160,15 @@ class _ShardedFunction(torch.autograd.Function):
     def backward(ctx, do):
         if do.stride(-1) != 1:
             do = do.contiguous()
-        q, kbuf, vbuf, o, lse = ctx.saved_tensors
+        q, kbuf, vbuf, o, lse, probs = ctx.saved_tensors
         spec, scale, plan, rank, group, ops = ctx.meta
         a0, _ = plan.owned(rank)
         lo = plan.lo[rank]
         L = plan.world * plan.rows_per_rank
         dq, dkb, dvb = ops.backward(q.transpose(1, 2), kbuf.permute(1, 2, 0, 3),
                                     vbuf.permute(1, 2, 0, 3), o, lse, do.transpose(1, 2), spec,
-                                    scale, row_offset=a0, kv_len=L, kv_offset=lo)
+                                    scale, row_offset=a0, kv_len=L, kv_offset=lo,
+                                    **({"probs": probs} if probs is not None else {}))
         # partial dK/dV per buffer row, back in the [rows, B, Hkv, D] order
         dk_rows = dkb.permute(2, 0, 1, 3)
         dv_rows = dvb.permute(2, 0, 1, 3)
