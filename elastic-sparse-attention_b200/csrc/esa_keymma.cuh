@@ -164,6 +164,47 @@ bwd_key_mma_kernel(const AttnParams p) {
     return c;
   };
 
+  // First slot q in [lo0, n) of column (k, t) whose key is >= target, given
+  // that slot lo0 - 1 (if any) is below it; starts at the guess g and
+  // gallops from there (down if g is already at or above the target, up
+  // otherwise), then bisects.  val = the key at the result (or INT_MAX at n).
+  auto find_first = [&](int lo0, int g, int target, int k, float t, int& val) {
+    int lo = lo0 - 1, hi = n, hv = 0x7fffffff;
+    if (lo0 < n) {
+      g = min(max(g, lo0), n - 1);
+      const int x = cidx(g, k, t);
+      if (x >= target) {
+        hi = g;
+        hv = x;
+        for (int step = 1; hi - step > lo; step <<= 1) {
+          const int y = cidx(hi - step, k, t);
+          if (y < target) { lo = hi - step; break; }
+          hi -= step;
+          hv = y;
+        }
+      } else {
+        lo = g;
+        for (int step = 1; lo + step < hi; step <<= 1) {
+          const int y = cidx(lo + step, k, t);
+          if (y >= target) { hi = lo + step; hv = y; break; }
+          lo += step;
+        }
+      }
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        const int y = cidx(mid, k, t);
+        if (y >= target) { hi = mid; hv = y; } else lo = mid;
+      }
+    }
+    val = hi < n ? hv : 0x7fffffff;
+    return hi;
+  };
+  // Approximate keys per query slot along a column (the index grows by
+  // (1 - alpha) + (k + t) * alpha / w per position), for the first guesses.
+  auto slope = [&](int k, float t) {
+    return fmaxf((1.f - p.pat.a) + (k + t) * p.pat.a / (float)w, 1e-6f);
+  };
+
   // Cursors: first query slot of each column whose key is >= the warp's first key.
   {
     const int P00 = p.kv_offset + lr0;
@@ -171,13 +212,14 @@ bwd_key_mma_kernel(const AttnParams p) {
       const int col = cc * 32 + lane;
       const Col c = column(col < ncols ? col : 0);
       if (col < ncols) {
-        int a = 0, e = n;
-        while (a < e) {
-          const int mid = (a + e) >> 1;
-          if (cidx(mid, c.k, c.t) < P00) a = mid + 1; else e = mid;
-        }
-        scur[col] = a;
-        sval[col] = a < n ? cidx(a, c.k, c.t) : 0x7fffffff;
+        // position whose key is about P00: st + (k + t) * sp - t = P00 with
+        // st = E (1 - alpha) - c and sp = (E alpha + c) / w, E = position + 1
+        const float num = (float)P00 + p.pat.c + c.t - (c.k + c.t) * p.pat.c / (float)w;
+        const float gq = num / slope(c.k, c.t) - 1.f - (float)p.row_offset;
+        const int g = (int)fminf(fmaxf(gq, 0.f), (float)n);
+        int v;
+        scur[col] = find_first(0, g, P00, c.k, c.t, v);
+        sval[col] = v;
       }
     }
   }
@@ -218,10 +260,10 @@ bwd_key_mma_kernel(const AttnParams p) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) { acck[i][e] = 0.f; accv[i][e] = 0.f; }
 
-    // Streams `total` users through the MMAs.  resolve(u, qi) -> Col of user
-    // u (and its query slot qi); every lane calls it; lane x and x + 16 both
-    // resolve user u0 + x.  The rows of batch i + 1 are in flight while batch
-    // i is multiplied, and batch i + 1's keys are computed meanwhile.
+    // Streams `total` users through the MMAs.  resolve(t0, qi) -> Col of
+    // user t0 + lane (and its query slot qi); every lane calls it, once per
+    // trip of 32 users, t0 = 0, 32, 64, ...  The rows of a batch are in flight
+    // while the previous batch is multiplied.
     auto stream = [&](const int total, auto&& resolve) {
       if (total <= 0) return;
       // One trip = 32 users (lane l: user t0 + l) = two batches of UB: users
@@ -235,19 +277,18 @@ bwd_key_mma_kernel(const AttnParams p) {
       int qi_f;
       Col c_f;
       auto fetch = [&](int t0, U& r) {   // resolve, start the (p, dS) load
-        const int u = t0 + lane;
-        c_f = resolve(u, qi_f);
-        r.pd = make_float2(0.f, 0.f);
-        r.oq = 0u;
-        r.od = 0u;
-        if (u < total) {
-          r.pd = p.pds[(int64_t)c_f.base * n + qi_f];
-          r.oq = (uint32_t)c_f.hh * qh16 + (uint32_t)qi_f * qs16;
-          r.od = (uint32_t)c_f.hh * dh16 + (uint32_t)qi_f * ds16;
-        }
+        const bool valid = t0 + lane < total;
+        c_f = resolve(t0, qi_f);
+        // past the end: slot 0 of column base 0 (in bounds), weights zeroed
+        if (!valid) { qi_f = 0; c_f.hh = 0; c_f.base = 0; }
+        const float2 pd = p.pds[(int64_t)c_f.base * n + qi_f];
+        r.pd = valid ? pd : make_float2(0.f, 0.f);
+        r.oq = (uint32_t)c_f.hh * qh16 + (uint32_t)qi_f * qs16;
+        r.od = (uint32_t)c_f.hh * dh16 + (uint32_t)qi_f * ds16;
       };
       auto key_of = [&](int t0) {
-        return t0 + lane < total ? cidx(qi_f, c_f.k, c_f.t) - P0 : 0;
+        const int key = cidx(qi_f, c_f.k, c_f.t) - P0;
+        return t0 + lane < total ? key : 0;
       };
       // start the row copies of half h of trip t0 into stage st
       auto copies = [&](int t0, int h, int st, const U& r) {
@@ -343,22 +384,10 @@ bwd_key_mma_kernel(const AttnParams p) {
         e = s;
         int ev = sval[col];
         if (ev < P1) {
-          // gallop to the first slot whose key is >= P1 (cidx(lo) < P1 throughout)
-          int lo = s, step = 1, hv = 0x7fffffff;
-          while (lo + step < n) {
-            const int x = cidx(lo + step, c.k, c.t);
-            if (x >= P1) { hv = x; break; }
-            lo += step;
-            step <<= 1;
-          }
-          int hi = min(lo + step, n);
-          while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            const int x = cidx(mid, c.k, c.t);
-            if (x >= P1) { hi = mid; hv = x; } else lo = mid;
-          }
-          e = hi;
-          ev = hi < n ? hv : 0x7fffffff;
+          // first slot after s whose key is >= P1, from the slope's guess
+          const float steps = (float)(P1 - ev) / slope(c.k, c.t);
+          const int g = s + (int)fminf(ceilf(steps), (float)n);
+          e = find_first(s + 1, g, P1, c.k, c.t, ev);
         }
         scur[col] = e;
         sval[col] = ev;
@@ -384,23 +413,37 @@ bwd_key_mma_kernel(const AttnParams p) {
     }
     __syncwarp();
 
-    // ---- B: the flat stream; user u -> the last column whose prefix is <= u,
-    // found by a short scan from this lane's previous column (a lane's users
-    // arrive in order), a binary search when the scan runs long
+    // ---- B: the flat stream; user u -> the last column whose prefix is <= u.
+    // Per trip (users t0 .. t0 + 31) the lanes load the prefixes of the 32
+    // columns after an anchor column c0 (prefix <= t0) and each lane counts,
+    // by a binary search over the lanes, those at or before its user.
     {
-      int hint = 0;
-      stream(run, [&](int u, int& qi) {
-        int col = hint, steps = 0;
-        while (steps < 8 && col + 1 < ncols && soff[col + 1] <= u) { ++col; ++steps; }
-        if (steps == 8 && col + 1 < ncols && soff[col + 1] <= u) {
-          int lo = col + 1, hi = ncols;   // soff[lo] <= u < soff[hi] (hi = ncols: end)
+      int c0 = 0;
+      // anchor c0: soff[c0] <= t0 at every trip
+      stream(run, [&](int t0, int& qi) {
+        const int u = t0 + lane;
+        const int cl = c0 + 1 + lane;
+        const int bl = cl < ncols ? soff[cl] : 0x7fffffff;
+        int col;
+        if (__ballot_sync(kAll, bl <= t0 + 31) != kAll) {
+          int pos = 0;   // window columns starting at or before u (bl is non-decreasing)
+#pragma unroll
+          for (int sh = 16; sh >= 1; sh >>= 1) {
+            const int v = __shfl_sync(kAll, bl, pos + sh - 1);
+            if (v <= u) pos += sh;
+          }
+          col = c0 + pos;
+          c0 += __popc(__ballot_sync(kAll, bl <= t0 + 32));
+        } else {
+          // more than 32 columns start inside the trip (empty columns): search
+          int lo = c0, hi = ncols;   // soff[lo] <= u < soff[hi] (hi = ncols: end)
           while (hi - lo > 1) {
             const int mid = (lo + hi) >> 1;
             if (soff[mid] <= u) lo = mid; else hi = mid;
           }
           col = lo;
+          c0 = __shfl_sync(kAll, col, 31);
         }
-        hint = col;
         qi = sst[col] + (u - soff[col]);
         return column(col);
       });
@@ -444,7 +487,8 @@ bwd_key_mma_kernel(const AttnParams p) {
           }
           const int total = __shfl_sync(kAll, off, 31);
           off -= len;
-          stream(total, [&](int u, int& qi) {
+          stream(total, [&](int t0, int& qi) {
+            const int u = t0 + lane;
             int o = 0;
 #pragma unroll
             for (int sh = 16; sh >= 1; sh >>= 1) {
