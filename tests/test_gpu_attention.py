@@ -506,16 +506,20 @@ def test_window_tensor_core_backward(esa, dtype, G, w, L, q_len):
         assert ((a.float() - b_.float()).abs() - 2 * HALF_ULP[dtype] * b_.float().abs()).max().item() < 2e-2, t
 
 
-@pytest.mark.parametrize("dtype,G,L,perm", [(torch.bfloat16, 4, 5000, False), (torch.float32, 2, 4100, False),
-                                            (torch.float32, 4, 3000, True)])
-def test_long_runs_split_into_chunks(esa, dtype, G, L, perm):
+@pytest.mark.parametrize("dtype,G,L,perm,D", [(torch.bfloat16, 4, 5000, False, 64),
+                                              (torch.bfloat16, 4, 5000, False, 128),
+                                              (torch.float16, 2, 4100, False, 128),
+                                              (torch.float32, 2, 4100, False, 64),
+                                              (torch.float32, 4, 3000, True, 64)])
+def test_long_runs_split_into_chunks(esa, dtype, G, L, perm, D):
     """alpha = 1 (last layer): head 0's slot 0 sends every query to key 0, and
     other heads' slot 0 has runs of thousands of queries.  Full 1024-slot
     chunks of such runs are summed by the chunk kernel and added by the key
-    side; gradients must match the oracle, also with unsorted query rows
-    (cache_position, sorted on the host with a permutation)."""
+    side (the tensor-core key kernel for 16-bit data in query order, the FMA
+    one otherwise); gradients must match the oracle, also with unsorted query
+    rows (cache_position, sorted on the host with a permutation)."""
     g = torch.Generator().manual_seed(L + G)
-    Hkv, D, nl = 2, 64, 8
+    Hkv, nl = 2, 8
     Hq = Hkv * G
     q, do = randn(1, Hq, L, D, dtype=dtype, gen=g), randn(1, Hq, L, D, dtype=dtype, gen=g)
     k, v = randn(1, Hkv, L, D, dtype=dtype, gen=g), randn(1, Hkv, L, D, dtype=dtype, gen=g)
@@ -524,3 +528,27 @@ def test_long_runs_split_into_chunks(esa, dtype, G, L, perm):
     ref = run_oracle(q, k, v, do, nl - 1, nl, 64, cache_position=cp)
     for got, want, t in zip((o, dq, dk, dv), ref, ("out", "dq", "dk", "dv")):
         assert_close(got, want, dtype, f"long runs {dtype} G{G} L{L} {t}")
+
+
+@pytest.mark.parametrize("dtype,G,D,layer", [(torch.bfloat16, 4, 128, 5), (torch.float16, 1, 128, 3),
+                                             (torch.bfloat16, 8, 64, 7), (torch.bfloat16, 2, 128, 1)])
+def test_key_side_tensor_core_matches_fma_kernel(esa, dtype, G, D, layer):
+    """The tensor-core key side (bf16 / fp16, D = 64 / 128, all heads of a KV
+    head in one launch, (p, dS) as hi + lo terms) against the FMA key kernel
+    (``gather_only``) on a longer sequence than the oracle cases: dK / dV within
+    two output ulps of each other."""
+    from elastic_sparse_attention_b200 import ops
+    g = torch.Generator().manual_seed(G * 31 + D + layer)
+    Hkv, L, w = 2, 6000, 64
+    Hq = Hkv * G
+    q, do = randn(1, Hq, L, D, dtype=dtype, gen=g), randn(1, Hq, L, D, dtype=dtype, gen=g)
+    k, v = randn(1, Hkv, L, D, dtype=dtype, gen=g), randn(1, Hkv, L, D, dtype=dtype, gen=g)
+    spec = ops.PatternSpec(layer, 8, w)
+    scale = D ** -0.5
+    o, lse = ops.forward(q, k, v, spec, scale)
+    _, dk_tc, dv_tc = ops.backward(q, k, v, o, lse, do, spec, scale)
+    _, dk_ga, dv_ga = ops.backward(q, k, v, o, lse, do, spec, scale, gather_only=True)
+    assert ops.device_errors() == 0
+    for a, b_, t in ((dk_tc, dk_ga, "dk"), (dv_tc, dv_ga, "dv")):
+        diff = (a.float() - b_.float()).abs() - 2 * HALF_ULP[dtype] * b_.float().abs()
+        assert diff.max().item() <= 1e-3, (t, diff.max().item())
