@@ -42,8 +42,8 @@ namespace esa {
 
 template <typename T, int D>
 struct KeyMma {
-  static constexpr int kWarps = 5;
-  static constexpr int kMinBlocks = 2;
+  static constexpr int kWarps = 4;
+  static constexpr int kMinBlocks = 3;
   static constexpr int kKeys = 4;                         // keys per tile (MMA N = 2 x 4)
   static constexpr int kUsers = 16;                       // MMA K
   static constexpr int kTiles = 8;                        // key tiles per warp
@@ -58,8 +58,8 @@ struct KeyMma {
   static constexpr int kMaxGroup = 16;                    // G (4 bits in the user word)
   static_assert(D == 64 || D == 128, "tensor-core key side is built for D = 64 and 128");
   static_assert(2 * kKeys * kEpRow * (int)sizeof(T) <= kRingBytes, "epilogue must fit the ring");
-  // ints of per-column state per warp (4 arrays), a multiple of 4
-  __host__ __device__ static constexpr int arrays(int cols) { return (4 * cols + 3) & ~3; }
+  // ints of per-column state per warp (2 arrays), a multiple of 4
+  __host__ __device__ static constexpr int arrays(int cols) { return (2 * cols + 3) & ~3; }
   static size_t smem_bytes(int cols) {
     return (size_t)kWarps * (kRingBytes + arrays(cols) * sizeof(int));
   }
@@ -132,12 +132,11 @@ bwd_key_mma_kernel(const AttnParams p) {
   const int w = p.pat.w, G = p.G;
   const int ncols = G * w, nrounds = (ncols + 31) >> 5;
   unsigned char* ring = smem_raw + warp * C::kRingBytes;
-  // per column: cursor, key at the cursor, this tile's first user slot, and
-  // the exclusive prefix of the tile's streamed user counts
+  // per column: the cursor (first query slot whose key is >= the current
+  // tile's first key; after step A of a tile, >= the next tile's) and the
+  // exclusive prefix of the tile's streamed user counts
   int* scur = reinterpret_cast<int*>(smem_raw + C::kWarps * C::kRingBytes) + warp * C::arrays(ncols);
-  int* sval = scur + ncols;
-  int* sst = sval + ncols;
-  int* soff = sst + ncols;
+  int* soff = scur + ncols;
   const int hkv = blockIdx.y, b = blockIdx.z;
   const int lr0 = (blockIdx.x * C::kWarps + warp) * (C::kTiles * NK);
   if (lr0 >= p.kv_rows) return;
@@ -205,23 +204,22 @@ bwd_key_mma_kernel(const AttnParams p) {
     return fmaxf((1.f - p.pat.a) + (k + t) * p.pat.a / (float)w, 1e-6f);
   };
 
+  // first query slot of column (k, t) whose key is >= P, searched from a guess:
+  // the position whose key is about P, st + (k + t) * sp - t = P with
+  // st = E (1 - alpha) - c and sp = (E alpha + c) / w, E = position + 1
+  auto first_user = [&](int P, int k, float t) {
+    const float num = (float)P + p.pat.c + t - (k + t) * p.pat.c / (float)w;
+    const float gq = num / slope(k, t) - 1.f - (float)p.row_offset;
+    const int g = (int)fminf(fmaxf(gq, 0.f), (float)n);
+    int v;
+    return find_first(0, g, P, k, t, v);
+  };
+
   // Cursors: first query slot of each column whose key is >= the warp's first key.
-  {
-    const int P00 = p.kv_offset + lr0;
-    for (int cc = 0; cc < nrounds; ++cc) {
-      const int col = cc * 32 + lane;
-      const Col c = column(col < ncols ? col : 0);
-      if (col < ncols) {
-        // position whose key is about P00: st + (k + t) * sp - t = P00 with
-        // st = E (1 - alpha) - c and sp = (E alpha + c) / w, E = position + 1
-        const float num = (float)P00 + p.pat.c + c.t - (c.k + c.t) * p.pat.c / (float)w;
-        const float gq = num / slope(c.k, c.t) - 1.f - (float)p.row_offset;
-        const int g = (int)fminf(fmaxf(gq, 0.f), (float)n);
-        int v;
-        scur[col] = find_first(0, g, P00, c.k, c.t, v);
-        sval[col] = v;
-      }
-    }
+  for (int cc = 0; cc < nrounds; ++cc) {
+    const int col = cc * 32 + lane;
+    const Col c = column(col < ncols ? col : 0);
+    if (col < ncols) scur[col] = first_user(p.kv_offset + lr0, c.k, c.t);
   }
 
   const unsigned char* qbytes = reinterpret_cast<const unsigned char*>(
@@ -382,15 +380,15 @@ bwd_key_mma_kernel(const AttnParams p) {
       if (ok) {
         s = scur[col];
         e = s;
-        int ev = sval[col];
+        const int ev = s < n ? cidx(s, c.k, c.t) : 0x7fffffff;   // key at the cursor
         if (ev < P1) {
           // first slot after s whose key is >= P1, from the slope's guess
           const float steps = (float)(P1 - ev) / slope(c.k, c.t);
           const int g = s + (int)fminf(ceilf(steps), (float)n);
-          e = find_first(s + 1, g, P1, c.k, c.t, ev);
+          int v;
+          e = find_first(s + 1, g, P1, c.k, c.t, v);
         }
         scur[col] = e;
-        sval[col] = ev;
         if (p.heavy_chunks > 0 && e - s >= kHeavyChunk) {
           const int cend = min(e / kHeavyChunk, p.heavy_chunks);
           for (int ch = (s + kHeavyChunk - 1) / kHeavyChunk; ch < cend && !heavy; ++ch)
@@ -404,10 +402,7 @@ bwd_key_mma_kernel(const AttnParams p) {
         const int y = __shfl_up_sync(kAll, off, o);
         if (lane >= o) off += y;
       }
-      if (ok) {
-        sst[col] = s;
-        soff[col] = run + off - len;
-      }
+      if (ok) soff[col] = run + off - len;
       run += __shfl_sync(kAll, off, 31);
       any_heavy |= __any_sync(kAll, heavy);
     }
@@ -424,7 +419,7 @@ bwd_key_mma_kernel(const AttnParams p) {
         const int u = t0 + lane;
         const int cl = c0 + 1 + lane;
         const int bl = cl < ncols ? soff[cl] : 0x7fffffff;
-        int col;
+        int col, nxt;   // nxt: prefix of the column after col
         if (__ballot_sync(kAll, bl <= t0 + 31) != kAll) {
           int pos = 0;   // window columns starting at or before u (bl is non-decreasing)
 #pragma unroll
@@ -433,6 +428,7 @@ bwd_key_mma_kernel(const AttnParams p) {
             if (v <= u) pos += sh;
           }
           col = c0 + pos;
+          nxt = min(__shfl_sync(kAll, bl, pos), run);   // soff[col + 1], run past the end
           c0 += __popc(__ballot_sync(kAll, bl <= t0 + 32));
         } else {
           // more than 32 columns start inside the trip (empty columns): search
@@ -442,9 +438,11 @@ bwd_key_mma_kernel(const AttnParams p) {
             if (soff[mid] <= u) lo = mid; else hi = mid;
           }
           col = lo;
+          nxt = col + 1 < ncols ? soff[col + 1] : run;
           c0 = __shfl_sync(kAll, col, 31);
         }
-        qi = sst[col] + (u - soff[col]);
+        // the column's users of this tile end at its cursor: [scur - len, scur)
+        qi = scur[col] - nxt + u;
         return column(col);
       });
     }
@@ -459,10 +457,11 @@ bwd_key_mma_kernel(const AttnParams p) {
         int cur = 0, e = 0;
         if (ok) {
           const int nxt = col + 1 < ncols ? soff[col + 1] : run;
-          if (nxt == soff[col]) {   // nothing streamed in B: empty or heavy
-            cur = sst[col];
-            e = scur[col];
-          }
+          e = scur[col];
+          if (nxt == soff[col] && e > 0)   // nothing streamed in B: empty or heavy
+            cur = first_user(P0, c.k, c.t);
+          else
+            cur = e;
         }
         while (__any_sync(kAll, cur < e)) {
           int seg_e = e, hc0 = 0, hc1 = 0;
