@@ -455,13 +455,23 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
   if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
     if (key_mma_path<T, D>(p)) {
       using KM = esa::KeyMma<T, D>;
-      const size_t smem = KM::smem_bytes(p.G * p.pat.w);
+      // one query head of each group per launch: a launch's working set (q /
+      // dO rows and the (p, dS) workspace of one head) stays near L2 size;
+      // the launches add up in the fp32 workspace, the last writes dK / dV
+      const int gs = p.acc ? KM::kHeadsPerLaunch : p.G;
+      const size_t smem = KM::smem_bytes(gs * p.pat.w);
       auto kern = esa::bwd_key_mma_kernel<T, D>;
       if (int rc = prepare_smem(kern, smem)) return rc;
       const int tile = KM::kWarps * KM::kTiles * KM::kKeys;
       dim3 grid((p.kv_rows + tile - 1) / tile, p.Hkv, p.B);
-      kern<<<grid, KM::kWarps * 32, smem, s>>>(p);
-      return check_launch("backward (key side, tensor cores)");
+      for (int h0 = 0; h0 < p.G; h0 += gs) {
+        esa::AttnParams pk = p;
+        pk.head_in_group = h0;
+        pk.key_heads = std::min(gs, p.G - h0);
+        kern<<<grid, KM::kWarps * 32, smem, s>>>(pk);
+        if (int rc = check_launch("backward (key side, tensor cores)")) return rc;
+      }
+      return ESA_OK;
     }
   }
   {

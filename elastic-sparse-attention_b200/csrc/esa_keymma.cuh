@@ -53,11 +53,12 @@ struct KeyMma {
   static constexpr int kUserBytes = 2 * kRowBytes;        // q row, then dO row
   static constexpr int kStageBytes = kUsers * kUserBytes;
   static constexpr int kRingBytes = 2 * kStageBytes;
-  static constexpr int kEpRow = D + 8;                    // epilogue row, padded (elements)
+  static constexpr int kEpRow = D + 4;                    // epilogue row (fp32), padded
   static constexpr int kMaxCols = 512;                    // G * w
   static constexpr int kMaxGroup = 16;                    // G (4 bits in the user word)
+  static constexpr int kHeadsPerLaunch = 1;               // with an fp32 workspace (G > 1)
   static_assert(D == 64 || D == 128, "tensor-core key side is built for D = 64 and 128");
-  static_assert(2 * kKeys * kEpRow * (int)sizeof(T) <= kRingBytes, "epilogue must fit the ring");
+  static_assert(2 * kKeys * kEpRow * (int)sizeof(float) <= kRingBytes, "epilogue must fit the ring");
   // ints of per-column state per warp (2 arrays), a multiple of 4
   __host__ __device__ static constexpr int arrays(int cols) { return (2 * cols + 3) & ~3; }
   static size_t smem_bytes(int cols) {
@@ -129,8 +130,9 @@ bwd_key_mma_kernel(const AttnParams p) {
   constexpr unsigned kAll = 0xffffffffu;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int w = p.pat.w, G = p.G;
-  const int ncols = G * w, nrounds = (ncols + 31) >> 5;
+  // this launch: query heads hh0 .. hh0 + GS - 1 of every group
+  const int w = p.pat.w, G = p.G, GS = p.key_heads, hh0 = p.head_in_group;
+  const int ncols = GS * w, nrounds = (ncols + 31) >> 5;
   unsigned char* ring = smem_raw + warp * C::kRingBytes;
   // per column: the cursor (first query slot whose key is >= the current
   // tile's first key; after step A of a tile, >= the next tile's) and the
@@ -144,8 +146,8 @@ bwd_key_mma_kernel(const AttnParams p) {
   const int kvmax = p.kv_len - 1;
   // col -> (hh, k) with hh = col / w by a multiply-high (exact for col < 2^14, w <= 1024)
   const unsigned long long wmagic = 0xffffffffull / (unsigned)w + 1ull;
-  // lane hh (< G) holds the head weight of query head hkv * G + hh
-  const float lane_t = head_weight(p.pat, hkv * G + (lane < G ? lane : 0));
+  // lane j (< GS) holds the head weight of query head hkv * G + hh0 + j
+  const float lane_t = head_weight(p.pat, hkv * G + hh0 + (lane < GS ? lane : 0));
   auto cidx = [&](int jq, int k, float t) -> int {
     return min(raw_index(row_window(p.pat, p.row_offset + jq), k, t, __fsub_rn(1.f, t)), kvmax);
   };
@@ -156,9 +158,10 @@ bwd_key_mma_kernel(const AttnParams p) {
   };
   auto column = [&](int col) {
     Col c;
-    c.hh = (int)(((unsigned long long)(unsigned)col * wmagic) >> 32);
-    c.k = col - c.hh * w;
-    c.t = __shfl_sync(kAll, lane_t, c.hh & 31);
+    const int j = (int)(((unsigned long long)(unsigned)col * wmagic) >> 32);
+    c.hh = hh0 + j;
+    c.k = col - j * w;
+    c.t = __shfl_sync(kAll, lane_t, j & 31);
     c.base = (b * p.Hq + hkv * G + c.hh) * w + c.k;
     return c;
   };
@@ -533,8 +536,9 @@ bwd_key_mma_kernel(const AttnParams p) {
       }
     }
 
-    // ---- epilogue: hi + lo columns (lanes t4 and t4 ^ 2), then [2][4 keys][D]
-    // in T (ring, drained) -> global
+    // ---- epilogue: hi + lo columns (lanes t4 and t4 ^ 2) -> fp32 [2][4 keys][D]
+    // in the ring (drained) -> global: dK / dV in T by the launch holding the
+    // group's last heads, the fp32 sum of the heads so far otherwise
     {
 #pragma unroll
       for (int i = 0; i < MT; ++i)
@@ -543,36 +547,48 @@ bwd_key_mma_kernel(const AttnParams p) {
           acck[i][e] += __shfl_xor_sync(kAll, acck[i][e], 2);
           accv[i][e] += __shfl_xor_sync(kAll, accv[i][e], 2);
         }
-      T* ep = reinterpret_cast<T*>(ring);
+      float* ep = reinterpret_cast<float*>(ring);
       if (t4 < 2) {
         const int k0 = 2 * t4;
 #pragma unroll
         for (int i = 0; i < MT; ++i) {
           const int d0 = 16 * i + g4;
-          ep[k0 * C::kEpRow + d0] = round_to<T>(acck[i][0]);
-          ep[(k0 + 1) * C::kEpRow + d0] = round_to<T>(acck[i][1]);
-          ep[k0 * C::kEpRow + d0 + 8] = round_to<T>(acck[i][2]);
-          ep[(k0 + 1) * C::kEpRow + d0 + 8] = round_to<T>(acck[i][3]);
-          ep[(NK + k0) * C::kEpRow + d0] = round_to<T>(accv[i][0]);
-          ep[(NK + k0 + 1) * C::kEpRow + d0] = round_to<T>(accv[i][1]);
-          ep[(NK + k0) * C::kEpRow + d0 + 8] = round_to<T>(accv[i][2]);
-          ep[(NK + k0 + 1) * C::kEpRow + d0 + 8] = round_to<T>(accv[i][3]);
+          ep[k0 * C::kEpRow + d0] = acck[i][0];
+          ep[(k0 + 1) * C::kEpRow + d0] = acck[i][1];
+          ep[k0 * C::kEpRow + d0 + 8] = acck[i][2];
+          ep[(k0 + 1) * C::kEpRow + d0 + 8] = acck[i][3];
+          ep[(NK + k0) * C::kEpRow + d0] = accv[i][0];
+          ep[(NK + k0 + 1) * C::kEpRow + d0] = accv[i][1];
+          ep[(NK + k0) * C::kEpRow + d0 + 8] = accv[i][2];
+          ep[(NK + k0 + 1) * C::kEpRow + d0 + 8] = accv[i][3];
         }
       }
       __syncwarp();
-      constexpr int kOut = 2 * NK * C::kChunks;
+      const bool first = hh0 == 0, last = hh0 + GS == G;
+      const int64_t plane = (int64_t)p.B * p.Hkv * p.kv_rows * D;
+      constexpr int kQuads = D / 4;
+      constexpr int kOut = 2 * NK * kQuads;   // float4 pieces
 #pragma unroll
       for (int idx = lane; idx < kOut; idx += 32) {
-        const int tensor = idx / (NK * C::kChunks);
-        const int rem = idx - tensor * (NK * C::kChunks);
-        const int kr = rem / C::kChunks, ch = rem % C::kChunks;
+        const int tensor = idx / (NK * kQuads);
+        const int rem = idx - tensor * (NK * kQuads);
+        const int kr = rem / kQuads, qd = rem % kQuads;
         const int row = lt + kr;
         if (row < p.kv_rows) {
-          const uint4 val = *reinterpret_cast<const uint4*>(ep + (tensor * NK + kr) * C::kEpRow + ch * 8);
-          T* dst = tensor == 0
-                       ? reinterpret_cast<T*>(p.dk) + b * p.sdkb + hkv * p.sdkh + (int64_t)row * p.sdks
-                       : reinterpret_cast<T*>(p.dv) + b * p.sdvb + hkv * p.sdvh + (int64_t)row * p.sdvs;
-          *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(dst) + ch * 16) = val;
+          float4 v = *reinterpret_cast<const float4*>(ep + (tensor * NK + kr) * C::kEpRow + 4 * qd);
+          float* acc = p.acc + tensor * plane + (((int64_t)b * p.Hkv + hkv) * p.kv_rows + row) * D + 4 * qd;
+          if (!first) {
+            const float4 x = *reinterpret_cast<const float4*>(acc);
+            v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+          }
+          if (last) {
+            T* dst = tensor == 0
+                         ? reinterpret_cast<T*>(p.dk) + b * p.sdkb + hkv * p.sdkh + (int64_t)row * p.sdks
+                         : reinterpret_cast<T*>(p.dv) + b * p.sdvb + hkv * p.sdvh + (int64_t)row * p.sdvs;
+            *reinterpret_cast<uint2*>(dst + 4 * qd) = make_uint2(pack2<T>(v.x, v.y), pack2<T>(v.z, v.w));
+          } else {
+            *reinterpret_cast<float4*>(acc) = v;
+          }
         }
       }
       __syncwarp();

@@ -35,7 +35,8 @@ struct AttnParams {
   float* acc;       // workspace fp32 [2, B, Hkv, kv_rows, D] (only when G > 1)
   const int64_t* sorted_rows;  // optional positions sorted ascending (key side)
   const int64_t* row_perm;     // optional: sorted slot -> query row of the tensors
-  int head_in_group;           // key-side launch: which query head of each group
+  int head_in_group;           // key-side launch: (first) query head of each group
+  int key_heads;               // tensor-core key side: query heads per launch
   int* err;                    // optional device error word (bit flags)
   bool alpha_zero;             // layer_idx == 0: the pattern is a causal window of w keys
   int flags;                   // ESA_FLAG_* of the call
