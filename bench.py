@@ -33,6 +33,10 @@ import time
 
 import torch
 
+# Query heads of a group per key-side backward launch (KeyMma::kHeadsPerLaunch in
+# csrc/esa_keymma.cuh); used to count this bench's kernel launches.
+KEY_HEADS_PER_LAUNCH = 2
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -323,8 +327,8 @@ def bench_ours(args, world, rank, local):
         "roofline": roofline,
         # per step: layer 0 = window forward + 2 window backward kernels; layers
         # 1..7 = tile forward + query-side tile backward + long-run chunk kernel
-        # + G key-side launches
-        "gpu_launches": args.steps * (3 + (NL - 1) * (3 + HQ // HKV)),
+        # + the key-side launches (KEY_HEADS_PER_LAUNCH query heads of a group each)
+        "gpu_launches": args.steps * (3 + (NL - 1) * (3 + -(-(HQ // HKV) // KEY_HEADS_PER_LAUNCH))),
         "clocks": clocks.summary(),
         "e2e": e2e,
     }

@@ -455,9 +455,10 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
   if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
     if (key_mma_path<T, D>(p)) {
       using KM = esa::KeyMma<T, D>;
-      // one query head of each group per launch: a launch's working set (q /
-      // dO rows and the (p, dS) workspace of one head) stays near L2 size;
-      // the launches add up in the fp32 workspace, the last writes dK / dV
+      // kHeadsPerLaunch query heads of each group per launch: a launch's
+      // working set (q / dO rows and the (p, dS) workspace of its heads)
+      // stays within a few L2 sizes; the launches add up in the fp32
+      // workspace, the last writes dK / dV
       const int gs = p.acc ? KM::kHeadsPerLaunch : p.G;
       const size_t smem = KM::smem_bytes(gs * p.pat.w);
       auto kern = esa::bwd_key_mma_kernel<T, D>;

@@ -56,7 +56,7 @@ struct KeyMma {
   static constexpr int kEpRow = D + 4;                    // epilogue row (fp32), padded
   static constexpr int kMaxCols = 512;                    // G * w
   static constexpr int kMaxGroup = 16;                    // G (4 bits in the user word)
-  static constexpr int kHeadsPerLaunch = 1;               // with an fp32 workspace (G > 1)
+  static constexpr int kHeadsPerLaunch = 2;               // with an fp32 workspace (G > 1)
   static_assert(D == 64 || D == 128, "tensor-core key side is built for D = 64 and 128");
   static_assert(2 * kKeys * kEpRow * (int)sizeof(float) <= kRingBytes, "epilogue must fit the ring");
   // ints of per-column state per warp (2 arrays), a multiple of 4
