@@ -21,19 +21,21 @@
 // so the eight rows an ldmatrix phase reads sit in distinct banks) and read
 // back transposed with ldmatrix.x4.trans, which yields the A fragments.
 //
-// Users are found per (head of the group, slot) column: the index is
-// non-decreasing along query positions, so a column's users of the keys
-// [P0, P0 + 4) are one contiguous query range [a, b); a is the cursor left by
-// the previous tile and b is found by galloping.  All G query heads of a KV
-// head run in the same warp, so dK / dV are written once in the input type.
-// Query chunks that use one key throughout (long runs, summed by
-// bwd_heavy_kernel) are skipped and their partial sums added.
+// Users are found per (head, slot) column: the index is non-decreasing along
+// query positions, so a column's users of the keys [P0, P0 + 4) are one
+// contiguous query range [a, b); a is the cursor left by the previous tile
+// and b is found by galloping from a slope-based guess.  A launch covers
+// kHeadsPerLaunch query heads of every group (its working set of q / dO rows
+// and (p, dS) columns stays within a few L2 sizes); with more heads per
+// group the launches add up in the fp32 workspace and the last one writes
+// dK / dV in the input type.  Query chunks that use one key throughout (long
+// runs, summed by bwd_heavy_kernel) are skipped and their partial sums added.
 //
 // Per tile: (A) every column's user range and a flat prefix of the counts,
-// (B) all those users in one software pipeline (user u -> column by a short
-// forward scan of the prefix from the lane's previous column), (C) the rare
-// columns holding summed chunks.  Warp = kTiles consecutive tiles of 4 keys;
-// CTA = kWarps warps.
+// (B) all those users in one software pipeline, 32 per trip (user u ->
+// column by a binary search over a 32-column window of the prefix), (C) the
+// rare columns holding summed chunks.  Warp = kTiles consecutive tiles of 4
+// keys; CTA = kWarps warps.
 #pragma once
 #include "esa_common.cuh"
 #include "esa_params.h"
