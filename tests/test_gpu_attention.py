@@ -531,12 +531,14 @@ def test_long_runs_split_into_chunks(esa, dtype, G, L, perm, D):
 
 
 @pytest.mark.parametrize("dtype,G,D,layer", [(torch.bfloat16, 4, 128, 5), (torch.float16, 1, 128, 3),
-                                             (torch.bfloat16, 8, 64, 7), (torch.bfloat16, 2, 128, 1)])
+                                             (torch.bfloat16, 8, 64, 7), (torch.bfloat16, 2, 128, 1),
+                                             (torch.bfloat16, 3, 128, 4)])
 def test_key_side_tensor_core_matches_fma_kernel(esa, dtype, G, D, layer):
-    """The tensor-core key side (bf16 / fp16, D = 64 / 128, all heads of a KV
-    head in one launch, (p, dS) as hi + lo terms) against the FMA key kernel
-    (``gather_only``) on a longer sequence than the oracle cases: dK / dV within
-    two output ulps of each other."""
+    """The tensor-core key side (bf16 / fp16, D = 64 / 128, two query heads of
+    a group per launch with fp32 sums between launches -- G = 3 ends with a
+    one-head launch -- and (p, dS) as hi + lo terms) against the FMA key
+    kernel (``gather_only``) on a longer sequence than the oracle cases: dK /
+    dV within two output ulps of each other."""
     from elastic_sparse_attention_b200 import ops
     g = torch.Generator().manual_seed(G * 31 + D + layer)
     Hkv, L, w = 2, 6000, 64
