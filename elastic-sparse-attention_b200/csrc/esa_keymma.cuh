@@ -48,7 +48,7 @@ struct KeyMma {
   static constexpr int kMinBlocks = 3;
   static constexpr int kKeys = 4;                         // keys per tile (MMA N = 2 x 4)
   static constexpr int kUsers = 16;                       // MMA K
-  static constexpr int kTiles = 8;                        // key tiles per warp
+  static constexpr int kTiles = 4;                        // key tiles per warp
   static constexpr int kRowBytes = D * (int)sizeof(T);
   static constexpr int kChunks = kRowBytes / 16;          // 16-byte chunks per row
   static constexpr int kUsersPerCopy = 32 / kChunks;      // users one cp.async step covers
