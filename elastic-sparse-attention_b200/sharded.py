@@ -94,12 +94,12 @@ def _exchange(plan: ShardPlan, rank: int, group, local: torch.Tensor, buf: torch
     a0, _ = plan.owned(rank)
     p2p = []
     for (q, a, b) in plan.pieces_needed(rank):
-        p2p.append(dist.P2POp(dist.irecv, buf[a - lo:b - lo], q, group))
+        p2p.append(dist.P2POp(dist.irecv, buf[a - lo:b - lo], group=group, group_peer=q))
     sends = []
     for (r, a, b) in plan.pieces_sent(rank):
         piece = local[a - a0:b - a0].contiguous()
         sends.append(piece)
-        p2p.append(dist.P2POp(dist.isend, piece, r, group))
+        p2p.append(dist.P2POp(dist.isend, piece, group=group, group_peer=r))
     if p2p:
         for req in dist.batch_isend_irecv(p2p):
             req.wait()
@@ -113,11 +113,12 @@ def _reverse_exchange(plan: ShardPlan, rank: int, group, dbuf: torch.Tensor, lo:
     a0, _ = plan.owned(rank)
     p2p, recvs = [], []
     for (q, a, b) in plan.pieces_needed(rank):
-        p2p.append(dist.P2POp(dist.isend, dbuf[a - lo:b - lo].contiguous(), q, group))
+        p2p.append(dist.P2POp(dist.isend, dbuf[a - lo:b - lo].contiguous(), group=group,
+                                   group_peer=q))
     for (r, a, b) in plan.pieces_sent(rank):
         t = torch.empty((b - a,) + tuple(dbuf.shape[1:]), dtype=dbuf.dtype, device=dbuf.device)
         recvs.append((t, a, b))
-        p2p.append(dist.P2POp(dist.irecv, t, r, group))
+        p2p.append(dist.P2POp(dist.irecv, t, group=group, group_peer=r))
     if p2p:
         for req in dist.batch_isend_irecv(p2p):
             req.wait()

@@ -53,27 +53,36 @@ class OracleOps:
         return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
 
 
-def _worker(rank, world, port, layer, S, Hq, Hkv, D, w, result_q):
+def _worker(rank, world, port, layer, S, Hq, Hkv, D, w, result_q, group_ranks=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     import elastic_sparse_attention_b200 as esa
-    L = S * world
+    # the sequence group: all ranks, or a sub-group (every rank takes part in
+    # creating it; ranks outside it do no attention work)
+    group = dist.new_group(group_ranks) if group_ranks is not None else None
+    members = group_ranks if group_ranks is not None else list(range(world))
+    if rank not in members:
+        dist.barrier()
+        dist.destroy_process_group()
+        return
+    grank, gworld = dist.get_rank(group), dist.get_world_size(group)
+    L = S * gworld
     g = torch.Generator().manual_seed(3)
     q, k, v, do = (torch.randn(1, L, h, D, generator=g) for h in (Hq, Hkv, Hkv, Hq))
-    sl = slice(rank * S, (rank + 1) * S)
+    sl = slice(grank * S, (grank + 1) * S)
     qs, ks, vs = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
     m = esa.SequenceShardedElasticSparseAttention(layer, 8, Hq, D, w, L, num_key_value_heads=Hkv,
-                                                  ops=OracleOps)
+                                                  group=group, ops=OracleOps)
     out = m(qs, ks, vs)
     out.backward(do[:, sl].reshape(1, S, Hq * D))
     parts = [out.detach(), qs.grad, ks.grad, vs.grad]
     gathered = []
     for t in parts:
-        lst = [torch.zeros_like(t) for _ in range(world)]
-        dist.all_gather(lst, t.contiguous())
+        lst = [torch.zeros_like(t) for _ in range(gworld)]
+        dist.all_gather(lst, t.contiguous(), group=group)
         gathered.append(torch.cat(lst, dim=1))
-    if rank == 0:
+    if grank == 0:
         idx, mask, _ = pattern.prepared_indices(Hq, w, layer, 8, L, L, L)
         ro, rdq, rdk, rdv = naive.naive_forward_backward_manual(
             q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), do.transpose(1, 2),
@@ -94,14 +103,20 @@ def _free_port():
     return port
 
 
-@pytest.mark.parametrize("world,layer,S,Hq,Hkv,D,w", [(2, 7, 96, 4, 2, 16, 16),
-                                                     (3, 4, 80, 2, 2, 16, 32),
-                                                     (2, 0, 70, 2, 1, 8, 16)])
-def test_sequence_sharded_matches_unsharded(world, layer, S, Hq, Hkv, D, w):
+@pytest.mark.parametrize("world,layer,S,Hq,Hkv,D,w,group_ranks",
+                         [(2, 7, 96, 4, 2, 16, 16, None),
+                          (3, 4, 80, 2, 2, 16, 32, None),
+                          (2, 0, 70, 2, 1, 8, 16, None),
+                          # a sequence group that is not WORLD: peers are
+                          # addressed by their rank inside the group
+                          (3, 6, 64, 4, 2, 16, 16, [2, 1]),
+                          (4, 3, 64, 2, 1, 16, 16, [1, 3])])
+def test_sequence_sharded_matches_unsharded(world, layer, S, Hq, Hkv, D, w, group_ranks):
     ctx = mp.get_context("spawn")
     result_q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, layer, S, Hq, Hkv, D, w, result_q))
+    procs = [ctx.Process(target=_worker,
+                         args=(r, world, port, layer, S, Hq, Hkv, D, w, result_q, group_ranks))
              for r in range(world)]
     for p in procs:
         p.start()
