@@ -24,7 +24,8 @@ DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 EXPORTED = ("esa_version", "esa_last_error", "esa_device_errors", "esa_forward_writes_probs",
             "esa_pattern",
             "esa_pattern_audit", "esa_forward", "esa_backward_workspace_size", "esa_backward",
-            "esa_backward_noalloc",
+            "esa_backward_noalloc", "esa_trace_enable", "esa_trace_count", "esa_trace_read",
+            "esa_probe_gather",
             # decoder-layer harness (include/esa_layer.h)
             "esa_rmsnorm_forward", "esa_rmsnorm_backward_workspace_size", "esa_rmsnorm_backward",
             "esa_rope_apply", "esa_swiglu_forward", "esa_swiglu_backward")
@@ -49,9 +50,10 @@ class EsaProblem(ctypes.Structure):
                 ("kv_offset", ctypes.c_int64), ("kv_rows", ctypes.c_int64),
                 ("row_offset", ctypes.c_int64), ("rows", ctypes.c_void_p),
                 ("scale", ctypes.c_float), ("flags", ctypes.c_int32),
-                ("dropout_p", ctypes.c_float), ("reserved", ctypes.c_int32),
+                ("dropout_p", ctypes.c_float), ("head_offset", ctypes.c_int32),
                 ("dropout_seed", ctypes.c_uint64), ("weights", ctypes.c_void_p),
-                ("probs", ctypes.c_void_p)]
+                ("probs", ctypes.c_void_p), ("pattern_heads", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
 
 
 class EsaError(RuntimeError):
@@ -97,6 +99,15 @@ def load() -> ctypes.CDLL:
                                      EsaTensor, P, EsaTensor, EsaTensor, EsaTensor, EsaTensor,
                                      P, P, P, ctypes.c_size_t, P]
         lib.esa_backward.restype = ctypes.c_int
+        lib.esa_trace_enable.argtypes = [i32]
+        lib.esa_trace_enable.restype = ctypes.c_int
+        lib.esa_trace_count.restype = ctypes.c_int
+        lib.esa_trace_read.argtypes = [i32, ctypes.POINTER(ctypes.c_char_p),
+                                       ctypes.POINTER(ctypes.c_float)]
+        lib.esa_trace_read.restype = ctypes.c_int
+        lib.esa_probe_gather.argtypes = [i32, ctypes.POINTER(EsaProblem), EsaTensor, EsaTensor,
+                                         P, P]
+        lib.esa_probe_gather.restype = ctypes.c_int
         F = ctypes.c_float
         lib.esa_rmsnorm_forward.argtypes = [i32, i64, i32, P, P, P, P, F, P, P, P]
         lib.esa_rmsnorm_forward.restype = ctypes.c_int
@@ -143,10 +154,24 @@ def problem(*, dtype: torch.dtype, batch: int, num_heads: int, num_kv_heads: int
             rows: torch.Tensor | None = None, scale: float, flags: int = 0,
             dropout_p: float = 0.0, dropout_seed: int = 0,
             weights: torch.Tensor | None = None,
-            probs: torch.Tensor | None = None) -> EsaProblem:
+            probs: torch.Tensor | None = None, head_offset: int = 0,
+            pattern_heads: int = 0) -> EsaProblem:
     if dtype not in DTYPES:
         raise TypeError(f"unsupported dtype {dtype}; expected float32, bfloat16 or float16")
     return EsaProblem(DTYPES[dtype], batch, num_heads, num_kv_heads, head_dim, attn_length,
                       layer_idx, num_hidden_layers, q_len, kv_len, kv_offset,
                       kv_len if kv_rows is None else kv_rows, row_offset, ptr(rows), scale, flags,
-                      dropout_p, 0, dropout_seed, ptr(weights), ptr(probs))
+                      dropout_p, head_offset, dropout_seed, ptr(weights), ptr(probs),
+                      pattern_heads, 0)
+
+
+def trace_records() -> list[tuple[str, float]]:
+    """(kernel name, milliseconds) of every launch recorded since
+    esa_trace_enable(1); waits for each record's end event."""
+    lib = load()
+    out = []
+    for i in range(lib.esa_trace_count()):
+        name, ms = ctypes.c_char_p(), ctypes.c_float()
+        check(lib.esa_trace_read(i, ctypes.byref(name), ctypes.byref(ms)), "esa_trace_read")
+        out.append((name.value.decode(), float(ms.value)))
+    return out

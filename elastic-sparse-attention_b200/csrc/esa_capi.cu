@@ -8,11 +8,13 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <mutex>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <vector>
 
 #include "esa_b200.h"
 #include "esa_layer.h"
@@ -21,6 +23,7 @@
 #include "esa_keymma.cuh"
 #include "esa_layer.cuh"
 #include "esa_pattern.cuh"
+#include "esa_probe.cuh"
 #include "esa_window_tc.cuh"
 #include "esa_window_bwd.cuh"
 
@@ -47,7 +50,8 @@ int check_launch(const char* what) {
 constexpr int64_t kMaxPosition = int64_t(1) << 24;  // float32 index math is exact below 2^24
 constexpr int kMaxAttnLength = 2048;
 
-esa::Pattern make_pattern(int num_heads, int w, int layer_idx, int num_hidden_layers) {
+esa::Pattern make_pattern(int num_heads, int w, int layer_idx, int num_hidden_layers,
+                          int head_offset = 0) {
   esa::Pattern P;
   const int denominator = num_hidden_layers > 1 ? num_hidden_layers - 1 : 1;   // :488
   const double alpha = (double)layer_idx / (double)denominator;                // :489
@@ -55,8 +59,59 @@ esa::Pattern make_pattern(int num_heads, int w, int layer_idx, int num_hidden_la
   P.num_heads = num_heads;
   P.a = (float)alpha;
   P.c = (float)((double)w * (1.0 - alpha));                                    // :496
-  P.inv_hm1 = 0.f;
+  P.head_offset = head_offset;
   return P;
+}
+
+// Query heads of the pattern a problem's heads belong to.
+int pattern_heads(const esa_problem_t* pb) {
+  return pb->pattern_heads > 0 ? pb->pattern_heads : pb->num_heads;
+}
+
+// ---- launch trace ----------------------------------------------------------
+// While enabled, every launch below is bracketed by two events recorded on its
+// stream (esa_trace_* in include/esa_b200.h).
+struct TraceRec {
+  const char* name;
+  cudaEvent_t a, b;
+};
+std::mutex g_trace_mu;
+std::atomic<bool> g_trace_on{false};
+std::vector<TraceRec> g_trace;
+
+class LaunchTrace {
+ public:
+  LaunchTrace(const char* name, cudaStream_t s) : s_(s) {
+    if (!g_trace_on.load(std::memory_order_relaxed)) return;
+    TraceRec r{name, nullptr, nullptr};
+    if (cudaEventCreate(&r.a) != cudaSuccess) return;
+    if (cudaEventCreate(&r.b) != cudaSuccess) {
+      cudaEventDestroy(r.a);
+      return;
+    }
+    cudaEventRecord(r.a, s);
+    std::lock_guard<std::mutex> lock(g_trace_mu);
+    g_trace.push_back(r);
+    end_ = r.b;
+  }
+  ~LaunchTrace() {
+    if (end_) cudaEventRecord(end_, s_);
+  }
+  LaunchTrace(const LaunchTrace&) = delete;
+  LaunchTrace& operator=(const LaunchTrace&) = delete;
+
+ private:
+  cudaStream_t s_;
+  cudaEvent_t end_ = nullptr;
+};
+
+void trace_clear() {
+  std::lock_guard<std::mutex> lock(g_trace_mu);
+  for (auto& r : g_trace) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  g_trace.clear();
 }
 
 int elem_size(int dtype) { return dtype == ESA_DTYPE_F32 ? 4 : 2; }
@@ -108,6 +163,11 @@ int check_problem(const esa_problem_t* pb) {
     return fail(ESA_ERR_INVALID, "weights must be 4-byte aligned");
   if (pb->probs && reinterpret_cast<uintptr_t>(pb->probs) % 16)
     return fail(ESA_ERR_INVALID, "probs must be 16-byte aligned");
+  if (pb->head_offset < 0 || pb->pattern_heads < 0 ||
+      (int64_t)pb->head_offset + pb->num_heads > pattern_heads(pb) || pattern_heads(pb) > 65535)
+    return fail(ESA_ERR_INVALID,
+                "head_offset %d + num_heads %d must be <= pattern_heads %d (<= 65535)",
+                pb->head_offset, pb->num_heads, pattern_heads(pb));
   return ESA_OK;
 }
 
@@ -124,7 +184,8 @@ esa::AttnParams base_params(const esa_problem_t* pb) {
   p.kv_rows = (int)pb->kv_rows;
   p.row_offset = (int)pb->row_offset;
   p.rows = pb->rows;
-  p.pat = make_pattern(pb->num_heads, pb->attn_length, pb->layer_idx, pb->num_hidden_layers);
+  p.pat = make_pattern(pattern_heads(pb), pb->attn_length, pb->layer_idx, pb->num_hidden_layers,
+                       pb->head_offset);
   p.scale = pb->scale;
   p.scale_log2 = pb->scale * esa::kLog2e;
   p.alpha_zero = pb->layer_idx == 0;   // alpha = layer_idx / max(nl - 1, 1) == 0
@@ -331,6 +392,7 @@ int launch_window(const esa::AttnParams& p, cudaStream_t s) {
                            esa::kWinSmemBytes) != cudaSuccess)
     return fail(ESA_ERR_CUDA, "cannot reserve shared memory for the window path");
   dim3 grid((p.n_rows + QT - 1) / QT, p.Hkv * (p.G / HT), p.B);
+  LaunchTrace tr("window_fwd_tc", s);
   kern<<<grid, esa::kWinThreads, esa::kWinSmemBytes, s>>>(maps, p, nk);
   return check_launch("forward (tensor-core window)");
 }
@@ -363,10 +425,16 @@ int launch_window_bwd(const esa::AttnParams& p, cudaStream_t s) {
                            esa::kWbkSmemBytes) != cudaSuccess)
     return fail(ESA_ERR_CUDA, "cannot reserve shared memory for the window backward");
   dim3 gq((p.n_rows + QT - 1) / QT, p.Hkv * (p.G / HT), p.B);
-  kq<<<gq, esa::kWinBwdThreads, esa::kWbqSmemBytes, s>>>(a, p, nk, delta);
+  {
+    LaunchTrace tr("window_bwd_dq_tc", s);
+    kq<<<gq, esa::kWinBwdThreads, esa::kWbqSmemBytes, s>>>(a, p, nk, delta);
+  }
   if (int rc = check_launch("backward (tensor-core window, dQ)")) return rc;
   dim3 gk((p.kv_rows + esa::kWbkKeys - 1) / esa::kWbkKeys, p.Hkv, p.B);
-  kkv<<<gk, esa::kWinBwdThreads, esa::kWbkSmemBytes, s>>>(b, p, delta);
+  {
+    LaunchTrace tr("window_bwd_dkv_tc", s);
+    kkv<<<gk, esa::kWinBwdThreads, esa::kWbkSmemBytes, s>>>(b, p, delta);
+  }
   return check_launch("backward (tensor-core window, dK dV)");
 }
 
@@ -388,6 +456,7 @@ int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
   }
   if (decode_path(p)) {
     const int nw = std::min((p.pat.w + 31) >> 5, esa::kDecodeMaxWarps);
+    LaunchTrace tr("fwd_decode", s);
     esa::fwd_decode_kernel<T, D><<<dim3(p.n_rows, p.Hq, p.B), nw * 32, 0, s>>>(p);
     return check_launch("forward (decode)");
   }
@@ -398,6 +467,7 @@ int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
       dim3 grid((p.n_rows + tq - 1) / tq, p.Hkv, p.B);
       auto kern = esa::fwd_tile_kernel<T, D>;
       if (int rc = prepare_smem(kern, esa::kTileSmemBytes)) return rc;
+      LaunchTrace tr("fwd_tile", s);
       kern<<<grid, 256, esa::kTileSmemBytes, s>>>(p);
       return check_launch("forward (tile)");
     }
@@ -408,6 +478,7 @@ int launch_forward(const esa::AttnParams& p, cudaStream_t s) {
   auto kern = esa::fwd_gather_kernel<T, D, kFwdWarps>;
   if (int rc = prepare_smem(kern, smem)) return rc;
   dim3 grid((p.n_rows + rpc - 1) / rpc, p.Hkv, p.B);
+  LaunchTrace tr("fwd_gather", s);
   kern<<<grid, kFwdWarps * 32, smem, s>>>(p, rpc);
   return check_launch("forward");
 }
@@ -432,7 +503,10 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
       dim3 grid((p.n_rows + tq - 1) / tq, p.Hkv, p.B);
       auto kern = esa::bwd_query_tile_kernel<T, D>;
       if (int rc = prepare_smem(kern, esa::kTileBwdSmemBytes)) return rc;
-      kern<<<grid, 256, esa::kTileBwdSmemBytes, s>>>(p);
+      {
+        LaunchTrace tr("bwd_query_tile", s);
+        kern<<<grid, 256, esa::kTileBwdSmemBytes, s>>>(p);
+      }
       if (int rc = check_launch("backward (query side, tile)")) return rc;
       query_done = true;
     }
@@ -444,12 +518,18 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
     auto kern = esa::bwd_query_kernel<T, D, kFwdWarps>;
     if (int rc = prepare_smem(kern, smem)) return rc;
     dim3 grid((p.n_rows + rpc - 1) / rpc, p.Hkv, p.B);
-    kern<<<grid, kFwdWarps * 32, smem, s>>>(p, rpc);
+    {
+      LaunchTrace tr("bwd_query", s);
+      kern<<<grid, kFwdWarps * 32, smem, s>>>(p, rpc);
+    }
     if (int rc = check_launch("backward (query side)")) return rc;
   }
   if (p.heavy_chunks > 0) {
     // partial sums of query chunks that all use one key (long runs)
-    esa::bwd_heavy_kernel<T, D><<<dim3(p.heavy_chunks, p.Hq, p.B), 256, 0, s>>>(p);
+    {
+      LaunchTrace tr("bwd_heavy", s);
+      esa::bwd_heavy_kernel<T, D><<<dim3(p.heavy_chunks, p.Hq, p.B), 256, 0, s>>>(p);
+    }
     if (int rc = check_launch("backward (key side, long runs)")) return rc;
   }
   if constexpr (!std::is_same<T, float>::value && (D == 64 || D == 128)) {
@@ -469,7 +549,10 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
         esa::AttnParams pk = p;
         pk.head_in_group = h0;
         pk.key_heads = std::min(gs, p.G - h0);
-        kern<<<grid, KM::kWarps * 32, smem, s>>>(pk);
+        {
+          LaunchTrace tr("bwd_key_mma", s);
+          kern<<<grid, KM::kWarps * 32, smem, s>>>(pk);
+        }
         if (int rc = check_launch("backward (key side, tensor cores)")) return rc;
       }
       return ESA_OK;
@@ -485,7 +568,10 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
     for (int gi = 0; gi < p.G; ++gi) {
       esa::AttnParams pk = p;
       pk.head_in_group = gi;
-      kern<<<grid, kKeyWarps * 32, smem, s>>>(pk);
+      {
+        LaunchTrace tr("bwd_key", s);
+        kern<<<grid, kKeyWarps * 32, smem, s>>>(pk);
+      }
       if (int rc = check_launch("backward (key side)")) return rc;
     }
   }
@@ -566,7 +652,7 @@ size_t acc_bytes(const esa_problem_t* pb) {
 
 extern "C" {
 
-int esa_version(void) { return 100; }
+int esa_version(void) { return 110; }
 
 const char* esa_last_error(void) { return g_last_error.c_str(); }
 
@@ -585,6 +671,7 @@ int esa_pattern(int32_t num_heads, int32_t attn_length, int32_t layer_idx,
   const int64_t total = (int64_t)num_heads * n_rows * attn_length;
   const int threads = 256;
   const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 64);
+  LaunchTrace tr("pattern", (cudaStream_t)stream);
   esa::pattern_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
       P, (int)n_rows, rows, (int)row_offset, (int)(clamp_len > 0 ? clamp_len : 0), idx, mask);
   return check_launch("esa_pattern");
@@ -601,6 +688,7 @@ int esa_pattern_audit(int32_t num_heads, int32_t attn_length, int32_t layer_idx,
   const int64_t total = (int64_t)num_heads * seq_len * attn_length;
   const int threads = 256;
   const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 32);
+  LaunchTrace tr("pattern_audit", (cudaStream_t)stream);
   esa::audit_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(P, (int)seq_len,
                                                                             d_count);
   return check_launch("esa_pattern_audit");
@@ -700,7 +788,97 @@ int esa_backward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_te
   return dispatch_op<BwdOp>(pb->dtype, pb->head_dim, p, (cudaStream_t)stream);
 }
 
+int esa_trace_enable(int32_t on) {
+  if (on) {
+    trace_clear();
+    g_trace_on.store(true);
+  } else {
+    g_trace_on.store(false);
+  }
+  return ESA_OK;
+}
+
+int esa_trace_count(void) {
+  std::lock_guard<std::mutex> lock(g_trace_mu);
+  return (int)g_trace.size();
+}
+
+int esa_trace_read(int32_t i, const char** name, float* ms) {
+  TraceRec r;
+  {
+    std::lock_guard<std::mutex> lock(g_trace_mu);
+    if (i < 0 || i >= (int32_t)g_trace.size()) return fail(ESA_ERR_INVALID, "esa_trace_read: no record %d", i);
+    r = g_trace[i];
+  }
+  if (name) *name = r.name;
+  if (ms) {
+    cudaError_t e = cudaEventSynchronize(r.b);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(ms, r.a, r.b);
+    if (e != cudaSuccess) return fail(ESA_ERR_CUDA, "esa_trace_read: %s", cudaGetErrorString(e));
+  }
+  return ESA_OK;
+}
+
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// esa_probe_gather: the tile forward's row loads alone (esa_probe.cuh).
+// ---------------------------------------------------------------------------
+namespace {
+
+struct ProbeOp {
+  template <typename T, int D>
+  static int run(const esa::AttnParams& p, cudaStream_t s, int mode, uint32_t* sink) {
+    if constexpr (std::is_same<T, float>::value || !(D == 64 || D == 128)) {
+      return fail(ESA_ERR_UNSUPPORTED, "esa_probe_gather: 16-bit data with head_dim 64 or 128 only");
+    } else {
+      if (!tile_path<T, D>(p))
+        return fail(ESA_ERR_UNSUPPORTED, "esa_probe_gather: the problem is not a tile-kernel problem");
+      if (mode == esa::kProbeL1Window && p.kv_rows < esa::kProbeWindowRows)
+        return fail(ESA_ERR_INVALID, "esa_probe_gather: the L1 window needs %d kv rows",
+                    esa::kProbeWindowRows);
+      const int tq = esa::kTilePairs / p.G;
+      dim3 grid((p.n_rows + tq - 1) / tq, p.Hkv, p.B);
+      auto kern = mode == esa::kProbePattern    ? esa::gather_probe_kernel<T, D, esa::kProbePattern>
+                  : mode == esa::kProbeL2Random ? esa::gather_probe_kernel<T, D, esa::kProbeL2Random>
+                                                : esa::gather_probe_kernel<T, D, esa::kProbeL1Window>;
+      if (int rc = prepare_smem(kern, esa::kTileSmemBytes)) return rc;
+      LaunchTrace tr("gather_probe", s);
+      kern<<<grid, 256, esa::kTileSmemBytes, s>>>(p, sink);
+      return check_launch("esa_probe_gather");
+    }
+  }
+};
+
+}  // namespace
+
+extern "C" int esa_probe_gather(int32_t mode, const esa_problem_t* pb, esa_tensor_t k,
+                                esa_tensor_t v, uint32_t* sink, void* stream) {
+  if (int rc = check_problem(pb)) return rc;
+  if (mode < ESA_PROBE_PATTERN || mode > ESA_PROBE_L1_WINDOW)
+    return fail(ESA_ERR_INVALID, "esa_probe_gather: unknown mode %d", mode);
+  if (!sink) return fail(ESA_ERR_INVALID, "esa_probe_gather: null sink");
+  if (pb->q_len == 0 || pb->batch == 0) return ESA_OK;
+  const int es = elem_size(pb->dtype);
+  if (int rc = check_tensor("k", k, es)) return rc;
+  if (int rc = check_tensor("v", v, es)) return rc;
+  esa::AttnParams p = base_params(pb);
+  if (int rc = device_error_word(&p.err)) return rc;
+  set_tensor(k, p.k, p.skb, p.skh, p.sks);
+  set_tensor(v, p.v, p.svb, p.svh, p.svs);
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (pb->dtype) {
+    case ESA_DTYPE_BF16:
+      if (pb->head_dim == 64) return ProbeOp::run<__nv_bfloat16, 64>(p, s, mode, sink);
+      if (pb->head_dim == 128) return ProbeOp::run<__nv_bfloat16, 128>(p, s, mode, sink);
+      break;
+    case ESA_DTYPE_F16:
+      if (pb->head_dim == 64) return ProbeOp::run<__half, 64>(p, s, mode, sink);
+      if (pb->head_dim == 128) return ProbeOp::run<__half, 128>(p, s, mode, sink);
+      break;
+  }
+  return fail(ESA_ERR_UNSUPPORTED, "esa_probe_gather: 16-bit data with head_dim 64 or 128 only");
+}
 
 // ---------------------------------------------------------------------------
 // esa_backward_noalloc: the backward with its workspace in a fixed array that

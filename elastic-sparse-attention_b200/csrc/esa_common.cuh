@@ -20,11 +20,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 // Per-layer constants of the pattern (reference :476-499).
 struct Pattern {
-  int w;          // attention_length
-  int num_heads;  // query heads H (the pattern is defined per query head)
-  float a;        // f32(alpha), alpha = layer_idx / max(nl - 1, 1)          :488-489
-  float c;        // f32(w * (1 - alpha)), the product taken in double        :496
-  float inv_hm1;  // unused by the bit-exact path; kept 0
+  int w;            // attention_length
+  int num_heads;    // query heads H of the pattern (it is defined per query head)
+  float a;          // f32(alpha), alpha = layer_idx / max(nl - 1, 1)          :488-489
+  float c;          // f32(w * (1 - alpha)), the product taken in double        :496
+  int head_offset;  // a launch's head h is pattern head head_offset + h (0 unless the
+                    // caller runs a subset of the heads, e.g. one GPU's share)
 };
 
 // Start and spacing of the window of one query position (reference :482-499).
@@ -50,9 +51,12 @@ __device__ __forceinline__ int oversized(const RowWin& r, int k) {
   return r.st + __float2int_rz(rintf(__fmul_rn(__int2float_rn(k), r.sp)));
 }
 
-// Head interpolation weight t = h / (H - 1) (reference :515-516).
+// Head interpolation weight t = h / (H - 1) (reference :515-516) of the
+// launch's head h, i.e. pattern head head_offset + h.
 __device__ __forceinline__ float head_weight(const Pattern& P, int h) {
-  return P.num_heads > 1 ? __fdiv_rn(__int2float_rn(h), __int2float_rn(P.num_heads - 1)) : 0.f;
+  return P.num_heads > 1
+             ? __fdiv_rn(__int2float_rn(h + P.head_offset), __int2float_rn(P.num_heads - 1))
+             : 0.f;
 }
 
 // Raw (unmasked, unclamped) index of slot k for a head with weight t:

@@ -140,7 +140,7 @@ fwd_gather_kernel(const AttnParams p, int rows_per_cta) {
       Sc e = M::scalar(exp2f(ssc[k] - mx));
       lsum += M::to_float(e);
       if (p.drop_threshold && k < w)   // dropout acts on the normalised weights (ref :674)
-        e = dropout_keep(p, pos, b * p.Hq + h, k) ? M::scalar(M::to_float(e) * p.keep_scale)
+        e = dropout_keep(p, pos, b, h, k) ? M::scalar(M::to_float(e) * p.keep_scale)
                                                    : M::scalar(0.f);
       sps[k] = e;
     }
@@ -639,7 +639,7 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
         if (p.drop_threshold) {
           // the same keep mask as the forward: dP = mask / (1 - p) * dO.v and
           // the weight used for dV is the kept, rescaled one
-          const bool keep = dropout_keep(p, pos, b * p.Hq + h, k);
+          const bool keep = dropout_keep(p, pos, b, h, k);
           dpk = keep ? dpk * p.keep_scale : 0.f;
           dsk = pk * (dpk - delta) * p.scale;
           pk = keep ? pk * p.keep_scale : 0.f;

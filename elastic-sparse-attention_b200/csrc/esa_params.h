@@ -41,7 +41,7 @@ struct AttnParams {
   bool alpha_zero;             // layer_idx == 0: the pattern is a causal window of w keys
   int flags;                   // ESA_FLAG_* of the call
   // Dropout of the softmax weights: keep when the Philox word of
-  // (position, batch * Hq + head, slot / 4) under key `seed` is >= threshold.
+  // (position, batch * H + pattern head, slot / 4) under key `seed` is >= threshold.
   uint32_t drop_threshold;     // 0 = no dropout
   float keep_scale;            // 1 / (1 - dropout_p)
   uint64_t seed;
@@ -56,8 +56,11 @@ struct AttnParams {
 
 constexpr int kHeavyChunk = 1024;
 
-__device__ __forceinline__ bool dropout_keep(const AttnParams& p, int pos, int bh, int k) {
-  const uint4 r = philox4x32_10(make_uint4((uint32_t)pos, (uint32_t)bh, (uint32_t)(k >> 2), 0u),
+// Keep decision of slot k of (position pos, batch b, launch head h); the
+// counter uses the pattern head, so a head split reproduces the same mask.
+__device__ __forceinline__ bool dropout_keep(const AttnParams& p, int pos, int b, int h, int k) {
+  const uint32_t bh = (uint32_t)(b * p.pat.num_heads + p.pat.head_offset + h);
+  const uint4 r = philox4x32_10(make_uint4((uint32_t)pos, bh, (uint32_t)(k >> 2), 0u),
                                 make_uint2((uint32_t)p.seed, (uint32_t)(p.seed >> 32)));
   const uint32_t word = (k & 3) == 0 ? r.x : (k & 3) == 1 ? r.y : (k & 3) == 2 ? r.z : r.w;
   return word >= p.drop_threshold;

@@ -1,0 +1,92 @@
+// Gather probe: the row loads of the slot-major tile forward without its
+// arithmetic, for measuring the row-gather bandwidth that bounds the gather
+// kernels (esa_probe_gather in include/esa_b200.h).
+//
+// Same grid, CTA shape and load order as fwd_tile_kernel: a CTA owns 128
+// (query, head) pairs of one KV head (128 / G queries x G heads), warp w owns
+// pairs [16w, 16w + 16), half a warp load is one 256-byte row; all warps walk
+// the slots together, K rows first (the score pass), then V rows (the P V
+// pass), two slots per step.  The rows come from the elastic pattern (the
+// tile kernels' exact stream), uniformly at random over the KV head's rows
+// (an L2-resident random gather), or at random within 64 rows per CTA (an
+// L1-resident gather).  The loaded words are folded into an xor checksum
+// that is stored only when it equals an improbable constant.
+#pragma once
+#include "esa_gather.cuh"
+
+namespace esa {
+
+enum ProbeMode : int { kProbePattern = 0, kProbeL2Random = 1, kProbeL1Window = 2 };
+constexpr int kProbeWindowRows = 64;
+
+// 32-bit integer mix (xor-shift / multiply rounds) for the random row choices.
+__device__ __forceinline__ uint32_t probe_mix(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
+template <typename T, int D, int MODE>
+__global__ void __launch_bounds__(256, 2)
+gather_probe_kernel(const AttnParams p, uint32_t* sink) {
+  using L = Layout<T, D>;
+  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  constexpr int PPW = kTilePairs / 8;      // pairs per warp
+  constexpr int MI = PPW / RPW;            // warp loads per slot
+  constexpr int HALF = kTileMaxW / 2;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int(*sidx)[kTileIdxStride] = reinterpret_cast<int(*)[kTileIdxStride]>(smem_raw);
+  const int w = p.pat.w;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane / LPR, r = lane % LPR;
+  const int G = p.G;
+  const int TQ = kTilePairs / G;
+  const int hkv = blockIdx.y, b = blockIdx.z;
+  const int j0 = blockIdx.x * TQ;
+  if (MODE == kProbePattern) {
+    const int pi = threadIdx.x >> 1;
+    tile_slot_rows(p, j0 + pi / G, hkv * G + pi % G, (threadIdx.x & 1) * HALF, HALF, &sidx[pi][0]);
+    __syncthreads();
+  }
+  const uint32_t cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  // L1 window: rows [win0, win0 + kProbeWindowRows), inside the buffer (the
+  // host requires kv_rows >= kProbeWindowRows)
+  const int win0 = MODE == kProbeL1Window
+                       ? (int)(probe_mix(cta) % (uint32_t)(p.kv_rows - kProbeWindowRows + 1))
+                       : 0;
+  auto row_at = [&](int pi, int k) -> int {
+    if (MODE == kProbePattern) return sidx[pi][k] & kRowMask;
+    const uint32_t hsh = probe_mix(cta * 8192u + (uint32_t)(pi * kTileMaxW + k));
+    if (MODE == kProbeL2Random) return (int)(hsh % (uint32_t)p.kv_rows);
+    return win0 + (int)(hsh & (kProbeWindowRows - 1));
+  };
+  const int pw0 = warp * PPW;
+  const T* Kb = reinterpret_cast<const T*>(p.k) + b * p.skb + hkv * p.skh + r * EPL;
+  const T* Vb = reinterpret_cast<const T*>(p.v) + b * p.svb + hkv * p.svh + r * EPL;
+  uint32_t acc = 0;
+#pragma unroll 1
+  for (int pass = 0; pass < 2; ++pass) {
+    const T* base = pass ? Vb : Kb;
+    const int64_t stride = pass ? p.svs : p.sks;
+    for (int k0 = 0; k0 < w; k0 += 2) {
+      uint4 x[2][MI];
+#pragma unroll
+      for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+        for (int m = 0; m < MI; ++m) {
+          const int k = min(k0 + s2, w - 1);
+          x[s2][m] = ldg16(base + (int64_t)row_at(pw0 + m * RPW + g, k) * stride);
+        }
+#pragma unroll
+      for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+        for (int m = 0; m < MI; ++m) acc ^= x[s2][m].x ^ x[s2][m].y ^ x[s2][m].z ^ x[s2][m].w;
+    }
+  }
+  if (acc == 0x9E3779B9u) *sink = acc;
+}
+
+}  // namespace esa

@@ -19,10 +19,23 @@ MAX_POSITION = 1 << 24
 
 @dataclass(frozen=True)
 class PatternSpec:
-    """The elastic pattern of one layer (reference __init__ arguments, :375-386)."""
+    """The elastic pattern of one layer (reference __init__ arguments, :375-386).
+
+    ``pattern_heads`` / ``head_offset``: the tensors of a call hold query heads
+    [head_offset, head_offset + Hq) of a layer with ``pattern_heads`` query
+    heads (the module's num_attention_heads); 0 / 0 = they hold every head.
+    Used to split one layer's heads over GPUs or launches."""
     layer_idx: int
     num_hidden_layers: int
     attention_length: int
+    pattern_heads: int = 0
+    head_offset: int = 0
+
+    def heads(self, pattern_heads: int, head_offset: int) -> "PatternSpec":
+        """The same layer's pattern for the query heads [head_offset, ...) of
+        ``pattern_heads``."""
+        return PatternSpec(self.layer_idx, self.num_hidden_layers, self.attention_length,
+                           pattern_heads, head_offset)
 
 
 def _aligned(t: torch.Tensor) -> bool:
@@ -104,7 +117,8 @@ def _problem(q, k, spec: PatternSpec, scale: float, rows, row_offset: int, kv_le
                         num_hidden_layers=spec.num_hidden_layers, q_len=Lq, kv_len=kv_len,
                         kv_offset=kv_offset, kv_rows=k.shape[2], row_offset=row_offset,
                         rows=rows, scale=scale, flags=flags, dropout_p=dropout_p,
-                        dropout_seed=dropout_seed, weights=weights, probs=probs)
+                        dropout_seed=dropout_seed, weights=weights, probs=probs,
+                        head_offset=spec.head_offset, pattern_heads=spec.pattern_heads)
 
 
 def probs_buffer(q, k, spec: PatternSpec, rows: torch.Tensor | None = None, row_offset: int = 0,

@@ -84,6 +84,15 @@ typedef struct {
  *                         and esa_backward, given the same buffer, reads them
  *                         instead of recomputing the scores (one gather pass
  *                         less).  NULL = the backward recomputes them.
+ *   head_offset,       -- the call's num_heads query heads are heads
+ *   pattern_heads         [head_offset, head_offset + num_heads) of a layer
+ *                         whose pattern is defined over pattern_heads query
+ *                         heads (the module's num_attention_heads, :375-386;
+ *                         the head weight is t = (head_offset + h) /
+ *                         (pattern_heads - 1), :515-516).  0 / 0 = the call
+ *                         holds every head.  This lets a caller split one
+ *                         layer's heads over GPUs or launches; num_kv_heads
+ *                         are then the K/V heads of those query heads.
  */
 typedef struct {
   int32_t dtype;
@@ -103,10 +112,12 @@ typedef struct {
   float scale;
   int32_t flags;   /* ESA_FLAG_* bits, 0 by default */
   float dropout_p;
-  int32_t reserved;
+  int32_t head_offset;
   uint64_t dropout_seed;
   void* weights;
   void* probs;
+  int32_t pattern_heads;
+  int32_t reserved;   /* 0 */
 } esa_problem_t;
 
 /* flags: run every layer on the CUDA-core gather kernels, also where the
@@ -122,7 +133,8 @@ typedef struct {
 #define ESA_DEVERR_QUERY_RANGE 4  /* a rows[] entry outside [-kv_len, kv_len);
                                      its output row is zero */
 
-/* Library version, e.g. 100 for 0.1.0. */
+/* Library version, e.g. 110 for 0.1.1 (110 added head_offset / pattern_heads
+ * to esa_problem_t, the launch trace and the gather probe). */
 int esa_version(void);
 
 /* Message of the last failing call on this thread ("" if none). */
@@ -199,6 +211,40 @@ int esa_backward(const esa_problem_t* prob, esa_tensor_t q, esa_tensor_t k, esa_
                  esa_tensor_t dk, esa_tensor_t dv, const int64_t* sorted_rows,
                  const int64_t* row_perm, void* workspace, size_t workspace_bytes,
                  void* stream);
+
+/*
+ * Launch trace (measurement aid; no reference counterpart).  While enabled,
+ * every kernel the library launches is bracketed by two CUDA events recorded
+ * on its stream, so a caller can attribute device time to the library's
+ * kernels without a profiler.  esa_trace_enable(1) clears the records and
+ * starts recording, esa_trace_enable(0) stops (records are kept);
+ * esa_trace_count() is the number of records; esa_trace_read(i, &name, &ms)
+ * waits for record i and gives its kernel's name and elapsed milliseconds.
+ * Recording creates CUDA events (no device memory) and is off by default.
+ */
+int esa_trace_enable(int32_t on);
+int esa_trace_count(void);
+int esa_trace_read(int32_t i, const char** name, float* ms);
+
+/*
+ * Gather probe (measurement aid; no reference counterpart): loads, without
+ * arithmetic, the K and V rows the slot-major tile forward would read for
+ * `prob` (16-bit data, head_dim 64 / 128, w <= 64; same grid, same order),
+ * B * num_heads * q_len * attn_length rows of each, and folds them into an
+ * xor checksum written to *sink (device uint32) only if it equals a fixed
+ * improbable value, so that the loads are not optimised away.  mode:
+ *   ESA_PROBE_PATTERN    the elastic pattern's rows (the tile kernels' stream)
+ *   ESA_PROBE_L2_RANDOM  the same number of rows, uniformly random over the
+ *                        KV head's kv_rows (one KV head at a time: L2-resident)
+ *   ESA_PROBE_L1_WINDOW  the same number of rows, random within 64 rows per
+ *                        CTA (K and V: 32 KB at D = 128, L1-resident)
+ * The elapsed time gives the achievable row-gather bandwidth of each level.
+ */
+#define ESA_PROBE_PATTERN 0
+#define ESA_PROBE_L2_RANDOM 1
+#define ESA_PROBE_L1_WINDOW 2
+int esa_probe_gather(int32_t mode, const esa_problem_t* prob, esa_tensor_t k, esa_tensor_t v,
+                     uint32_t* sink, void* stream);
 
 /* Size of the workspace array built into the library for esa_backward_noalloc. */
 #define ESA_NOALLOC_WORKSPACE_BYTES (16u * 1024u * 1024u)

@@ -43,8 +43,9 @@ def test_struct_layout_matches_header(tmp_path, esa):
         " offsetof(esa_problem_t, q_len), offsetof(esa_problem_t, rows),"
         " offsetof(esa_problem_t, scale), sizeof(esa_tensor_t),"
         " offsetof(esa_tensor_t, stride_s), offsetof(esa_problem_t, row_offset));\n"
-        ' printf(" %zu %zu %zu\\n", offsetof(esa_problem_t, dropout_seed),'
-        " offsetof(esa_problem_t, weights), offsetof(esa_problem_t, probs));\n"
+        ' printf(" %zu %zu %zu %zu %zu\\n", offsetof(esa_problem_t, dropout_seed),'
+        " offsetof(esa_problem_t, weights), offsetof(esa_problem_t, probs),"
+        " offsetof(esa_problem_t, head_offset), offsetof(esa_problem_t, pattern_heads));\n"
         " return 0; }\n")
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-std=c99", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)],
@@ -54,7 +55,7 @@ def test_struct_layout_matches_header(tmp_path, esa):
     P, T = esa._lib.EsaProblem, esa._lib.EsaTensor
     want = [ctypes.sizeof(P), P.q_len.offset, P.rows.offset, P.scale.offset, ctypes.sizeof(T),
             T.stride_s.offset, P.row_offset.offset, P.dropout_seed.offset, P.weights.offset,
-            P.probs.offset]
+            P.probs.offset, P.head_offset.offset, P.pattern_heads.offset]
     assert got == want
 
 
@@ -62,8 +63,8 @@ def _problem(esa, **kw):
     base = dict(dtype=esa._lib.DTYPES[__import__("torch").bfloat16], batch=1, num_heads=4,
                 num_kv_heads=2, head_dim=128, attn_length=64, layer_idx=3, num_hidden_layers=8,
                 q_len=16, kv_len=16, kv_offset=0, kv_rows=16, row_offset=0, rows=None,
-                scale=128 ** -0.5, flags=0, dropout_p=0.0, reserved=0, dropout_seed=0,
-                weights=None, probs=None)
+                scale=128 ** -0.5, flags=0, dropout_p=0.0, head_offset=0, dropout_seed=0,
+                weights=None, probs=None, pattern_heads=0, reserved=0)
     base.update(kw)
     return esa._lib.EsaProblem(**base)
 
@@ -76,6 +77,9 @@ def _problem(esa, **kw):
     (dict(kv_len=1 << 25), -2, "2^24"),
     (dict(dtype=7), -1, "dtype"),
     (dict(scale=float("inf")), -1, "scale"),
+    (dict(head_offset=1), -1, "head_offset"),
+    (dict(head_offset=2, pattern_heads=5), -1, "head_offset"),
+    (dict(head_offset=-1, pattern_heads=8), -1, "head_offset"),
 ])
 def test_forward_rejects_bad_problems(esa, kw, code, frag):
     lib = esa._lib.load()

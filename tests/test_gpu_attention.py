@@ -588,3 +588,36 @@ def test_sequence_split_kernel_offsets(esa, layer):
             assert_close(got, want, dt, f"split l{layer} rank {r} {t}")
         del o, lse, dq, dk, dv, ro, rdq, rdk, rdv, pr
     assert esa.ops.device_errors() == 0
+
+
+@pytest.mark.parametrize("dtype,layer,D", [(torch.bfloat16, 5, 128), (torch.float32, 3, 64),
+                                           (torch.bfloat16, 0, 128)])
+def test_head_split_matches_all_heads(esa, dtype, layer, D):
+    """A call on a subset of the query heads (PatternSpec.heads: the heads
+    [head_offset, head_offset + Hq) of a pattern over pattern_heads heads,
+    whole GQA groups with their K/V heads) gives exactly the slices of the
+    call on all heads: outputs, lse, gradients, and the dropout mask."""
+    g = torch.Generator().manual_seed(70 + layer)
+    B, Hq, Hkv, L, w = 1, 8, 4, 1100, 64   # > 4096 (row, head) pairs per share: no latency kernel
+    G = Hq // Hkv
+    q, do = randn(B, Hq, L, D, dtype=dtype, gen=g), randn(B, Hq, L, D, dtype=dtype, gen=g)
+    k, v = randn(B, Hkv, L, D, dtype=dtype, gen=g), randn(B, Hkv, L, D, dtype=dtype, gen=g)
+    spec = esa.PatternSpec(layer, 8, w)
+    scale = D ** -0.5
+    o, lse = esa.ops.forward(q, k, v, spec, scale)
+    dq, dk, dv = esa.ops.backward(q, k, v, o, lse, do, spec, scale)
+    _, _, wts = esa.ops.forward(q, k, v, spec, scale, dropout_p=0.2, dropout_seed=5,
+                                return_weights=True)
+    for kv0 in range(0, Hkv, 2):   # two shares of two KV heads each
+        h0, h1 = kv0 * G, (kv0 + 2) * G
+        sub = spec.heads(Hq, h0)
+        qs, dos = q[:, h0:h1].contiguous(), do[:, h0:h1].contiguous()
+        ks, vs = k[:, kv0:kv0 + 2].contiguous(), v[:, kv0:kv0 + 2].contiguous()
+        os_, lses = esa.ops.forward(qs, ks, vs, sub, scale)
+        dqs, dks, dvs = esa.ops.backward(qs, ks, vs, os_, lses, dos, sub, scale)
+        assert torch.equal(os_, o[:, h0:h1]) and torch.equal(lses, lse[:, h0:h1])
+        assert torch.equal(dqs, dq[:, h0:h1])
+        assert torch.equal(dks, dk[:, kv0:kv0 + 2]) and torch.equal(dvs, dv[:, kv0:kv0 + 2])
+        _, _, ws = esa.ops.forward(qs, ks, vs, sub, scale, dropout_p=0.2, dropout_seed=5,
+                                   return_weights=True)
+        assert torch.equal(ws, wts[:, h0:h1])
