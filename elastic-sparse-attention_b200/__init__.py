@@ -8,9 +8,11 @@ directory).
 from . import _lib, layer_ops, ops
 from .attention import ElasticSparseAttention, ElasticSparseAttentionFunction
 from .decoder import ElasticDecoderStack
+from .head_split import HeadShardedElasticSparseAttention, head_share
 from .ops import PatternSpec
 from .sharded import SequenceShardedElasticSparseAttention
 
 __all__ = ["ElasticSparseAttention", "ElasticSparseAttentionFunction", "ElasticDecoderStack",
-           "PatternSpec", "SequenceShardedElasticSparseAttention", "layer_ops", "ops", "_lib"]
+           "HeadShardedElasticSparseAttention", "PatternSpec",
+           "SequenceShardedElasticSparseAttention", "head_share", "layer_ops", "ops", "_lib"]
 __version__ = "0.1.0"

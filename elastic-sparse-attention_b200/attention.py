@@ -45,7 +45,9 @@ _audited: dict[tuple, int] = {}   # (H, w, layer, nl) -> longest audited sequenc
 
 def _ensure_monotone(num_heads: int, spec: PatternSpec, seq_len: int, device: torch.device):
     """The backward's key-side enumeration needs every per-slot index column to
-    be non-decreasing along positions; check it once per pattern and length."""
+    be non-decreasing along positions; check it once per pattern and length
+    (over all of the pattern's heads when the call holds a subset of them)."""
+    num_heads = spec.pattern_heads or num_heads
     key = (num_heads, spec.attention_length, spec.layer_idx, spec.num_hidden_layers)
     with _audit_lock:
         if _audited.get(key, 0) >= seq_len:

@@ -621,3 +621,30 @@ def test_head_split_matches_all_heads(esa, dtype, layer, D):
         _, _, ws = esa.ops.forward(qs, ks, vs, sub, scale, dropout_p=0.2, dropout_seed=5,
                                    return_weights=True)
         assert torch.equal(ws, wts[:, h0:h1])
+
+
+def test_head_sharded_module_matches_full_module(esa):
+    """HeadShardedElasticSparseAttention on each of 4 emulated ranks (one GPU)
+    gives its heads' columns of the full module's output and its heads'
+    gradients, bit for bit."""
+    g = torch.Generator().manual_seed(12)
+    B, Hq, Hkv, L, D, layer = 1, 16, 4, 1500, 128, 6
+    dt = torch.bfloat16
+    q, do = randn(B, Hq, L, D, dtype=dt, gen=g), randn(B, Hq, L, D, dtype=dt, gen=g)
+    k, v = randn(B, Hkv, L, D, dtype=dt, gen=g), randn(B, Hkv, L, D, dtype=dt, gen=g)
+    full = run_module(esa, q, k, v, do, layer, 8, 64)
+    world = 4
+    for r in range(world):
+        h0, nh, kv0, nkv = esa.head_share(Hq, Hkv, r, world)
+        m = esa.HeadShardedElasticSparseAttention(layer, 8, Hq, D, 64, L, num_key_value_heads=Hkv,
+                                                  rank=r, world_size=world)
+        qq = q[:, h0:h0 + nh].clone().requires_grad_(True)
+        kk = k[:, kv0:kv0 + nkv].clone().requires_grad_(True)
+        vv = v[:, kv0:kv0 + nkv].clone().requires_grad_(True)
+        out = m(qq, kk, vv)
+        out.backward(do[:, h0:h0 + nh].transpose(1, 2).reshape(B, L, nh * D))
+        o = out.detach().view(B, L, nh, D).transpose(1, 2)
+        assert torch.equal(o, full[0][:, h0:h0 + nh])
+        assert torch.equal(qq.grad, full[1][:, h0:h0 + nh])
+        assert torch.equal(kk.grad, full[2][:, kv0:kv0 + nkv])
+        assert torch.equal(vv.grad, full[3][:, kv0:kv0 + nkv])

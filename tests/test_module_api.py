@@ -87,3 +87,19 @@ def test_decoder_stack_builds_on_cpu(esa):
         esa.ElasticDecoderStack(hidden_size=64, num_attention_heads=4, num_key_value_heads=3,
                                 vocab_size=10, intermediate_size=8, dtype=torch.float32,
                                 device="cpu")
+
+
+def test_head_share_splits_whole_groups(esa):
+    """C3's head split: rank r of N holds Hkv / N whole GQA groups."""
+    shares = [esa.head_share(32, 8, r, 4) for r in range(4)]
+    assert shares == [(0, 8, 0, 2), (8, 8, 2, 2), (16, 8, 4, 2), (24, 8, 6, 2)]
+    assert esa.head_share(16, 16, 7, 8) == (14, 2, 14, 2)
+    with pytest.raises(ValueError, match="whole GQA groups"):
+        esa.head_share(32, 8, 0, 3)
+    with pytest.raises(ValueError, match="outside"):
+        esa.head_share(32, 8, 4, 4)
+    m = esa.HeadShardedElasticSparseAttention(3, 8, 32, 128, 64, 4096, num_key_value_heads=8,
+                                              rank=1, world_size=4)
+    assert m.pattern.head_offset == 8 and m.pattern.pattern_heads == 32
+    with pytest.raises(ValueError, match="holds 8 query / 2 KV heads"):
+        m(torch.randn(1, 4, 8, 128), torch.randn(1, 2, 8, 128), torch.randn(1, 2, 8, 128))
