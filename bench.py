@@ -2,22 +2,32 @@
 
 Workload (BASELINE.json metric, configuration C3): forward + backward of the
 8 layers of the elastic pattern P8 (attention_length=64, num_hidden_layers=8,
-layer_idx 0..7) at B=1 per GPU, 32 query heads / 8 KV heads, L=131072,
-head_dim=128, bf16, q/k/v/dO ~ N(0,1) from a seed (synthetic).  One step runs
-the 8 layers on the same inputs.  Inputs (2.5 GB per GPU) are larger than the
-126 MB L2, so no flush is needed between steps.
+layer_idx 0..7) for B=1, 32 query heads / 8 KV heads, L=131072, head_dim=128,
+bf16, q/k/v/dO ~ N(0,1) from a seed (synthetic).  One step runs the 8 layers
+on the same inputs.  Inputs (2.7 GB) are larger than the 126 MB L2, so no
+flush is needed between steps.
+
+N GPUs (torchrun): the same C3 problem is split by whole GQA groups (rank r
+computes KV heads [r*8/N, (r+1)*8/N) with their 4 query heads each, no
+collective; strong scaling); the time is the max over ranks.  The line also
+carries the weak-scaling figure (every rank runs the whole problem) and the
+C5 sequence-split figure (1M tokens, query rows split over the N ranks, the
+remote K/V fetched over NCCL) at the same N.
 
 Metric: effective TFLOP/s over active blocks =
     sum over layers of 3.5 * 4 * D * 128 * 128 * (#(128-query tile, 128-key
     block) pairs holding >= 1 valid (query, key) entry, over all heads)
 divided by the time; fwd counts 4*D per pair and bwd 10*D (x3.5 total).
-The line also reports ms/call, useful TFLOP/s (14 * D * valid pairs / time),
-per-kernel times, a roofline for the dominant kernel, the CPU baseline (the
-oracle port of the reference's naive path on a bounded row sample) and an
-end-to-end figure through the public module with host buffers.
+This counts every touched block as dense work; the dilated layers use
+0.5-2.5 % of a touched block, so it exceeds any dense peak by construction.
+The line therefore also reports useful TFLOP/s (14 * D * valid entries), the
+per-kernel-family device times (launch trace: CUDA events around every
+library launch), rooflines on compulsory HBM bytes, the measured row-gather
+ceiling (gather probe), C2 (forward only), the reference's own Triton kernel
+timed on the same GPU, the CPU baseline (the oracle port of the reference's
+naive path on a bounded row sample) and an end-to-end figure through the
+public module with host buffers.
 
-Multi-GPU (torchrun): batch split with no collective -- each rank runs its own
-B=1 instance (weak scaling); the time is the max over ranks.
 `--impl reference` times the reference's CPU path (oracle port) instead.
 """
 from __future__ import annotations
@@ -28,14 +38,11 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 
 import torch
-
-# Query heads of a group per key-side backward launch (KeyMma::kHeadsPerLaunch in
-# csrc/esa_keymma.cuh); used to count this bench's kernel launches.
-KEY_HEADS_PER_LAUNCH = 2
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -44,7 +51,13 @@ B, HQ, HKV, L, D, W, NL = 1, 32, 8, 131072, 128, 64, 8
 TILE = 128
 METRIC = "effective TFLOP/s (active blocks), fwd+bwd, 128k ctx"
 UNIT = "TFLOP/s"
-WORKLOAD = "C3: fwd+bwd of the 8 P8 layers (w=64, nl=8), B=1/GPU, 32q/8kv heads, L=131072, D=128, bf16"
+WORKLOAD = "C3: fwd+bwd of the 8 P8 layers (w=64, nl=8), B=1, 32q/8kv heads, L=131072, D=128, bf16"
+ES = 2   # bf16 bytes
+
+# C2 (forward only): B=2, 32 heads (MHA), L=32768, D=128, bf16, N(0,1) * D^-0.25
+C2_B, C2_H, C2_L = 2, 32, 32768
+# C5 (sequence split): B=1, 16 heads (MHA), L=2^20, D=128, bf16
+C5_H, C5_L = 16, 1 << 20
 
 
 def peaks():
@@ -66,6 +79,14 @@ def dist_init():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=torch.device("cuda", local))
     return world, rank, local
+
+
+def max_over_ranks(x: float, dev, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
 
 
 class ClockSampler:
@@ -155,13 +176,630 @@ def active_blocks_and_pairs(esa, dev):
     return out
 
 
-def make_inputs(dev, seed):
+def make_inputs(dev, seed, heads=(0, HQ), kv_heads=(0, HKV)):
+    """q, k, v, dO of the C3 problem (the same values at any split), restricted
+    to query heads [heads) and KV heads [kv_heads)."""
     g = torch.Generator(device=dev).manual_seed(seed)
     q = torch.randn(B, HQ, L, D, device=dev, generator=g).to(torch.bfloat16)
     k = torch.randn(B, HKV, L, D, device=dev, generator=g).to(torch.bfloat16)
     v = torch.randn(B, HKV, L, D, device=dev, generator=g).to(torch.bfloat16)
     do = torch.randn(B, HQ, L, D, device=dev, generator=g).to(torch.bfloat16)
+    if heads != (0, HQ):
+        q, do = (t[:, heads[0]:heads[1]].contiguous() for t in (q, do))
+        k, v = (t[:, kv_heads[0]:kv_heads[1]].contiguous() for t in (k, v))
     return q, k, v, do
+
+
+# ---------------------------------------------------------------------------
+# Kernel families and their bytes
+# ---------------------------------------------------------------------------
+FAMILY = {"window_fwd_tc": "fwd_window", "fwd_tile": "fwd_tile", "fwd_gather": "fwd_gather",
+          "fwd_decode": "fwd_decode", "window_bwd_dq_tc": "bwd_window",
+          "window_bwd_dkv_tc": "bwd_window", "bwd_query_tile": "bwd_query",
+          "bwd_query": "bwd_query", "bwd_heavy": "bwd_heavy", "bwd_key_mma": "bwd_key",
+          "bwd_key": "bwd_key"}
+
+
+def layer_bytes(nh, nkv, n=L, es=ES):
+    """Compulsory HBM bytes of one layer: forward reads q, k, v and writes o,
+    lse; backward reads q, o, dO, k, v, lse and writes dq, dk, dv."""
+    q_b, kv_b, lse_b = B * nh * n * D * es, B * nkv * n * D * es, B * nh * n * 4
+    return 2 * q_b + 2 * kv_b + lse_b, 4 * q_b + 4 * kv_b + lse_b
+
+
+def family_bytes(nh, nkv, key_heads_per_launch=2):
+    """Per layer and kernel family: (algorithmic bytes = what the family's
+    role must read and write, implementation bytes = this build's own
+    intermediates).  The tile forward leaves fp32 probabilities for the
+    backward; the query side reads them and writes (p, dS) per (row, slot);
+    the key side reads (p, dS) and, with GQA, sums its launches in fp32."""
+    q_b, kv_b, lse_b = B * nh * L * D * ES, B * nkv * L * D * ES, B * nh * L * 4
+    probs_b, pds_b = B * nh * W * L * 4, B * nh * W * L * 8
+    g = nh // nkv
+    launches = -(-g // key_heads_per_launch)
+    acc_b = 2 * (launches - 1) * 2 * B * nkv * L * D * 4 if g > 1 else 0
+    fwd, bwd = layer_bytes(nh, nkv)
+    return {"fwd_window": (fwd, 0), "fwd_tile": (fwd, probs_b),
+            "bwd_window": (bwd, 2 * lse_b),
+            "bwd_query": (3 * q_b + 2 * kv_b, probs_b + pds_b),
+            "bwd_key": (2 * q_b + 2 * kv_b, pds_b + acc_b),
+            "bwd_heavy": (0, 0)}
+
+
+def load_traffic():
+    """Measured DRAM bytes per layer and family (profiles/traffic.json)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+def trace_step(esa, fn):
+    """Run fn() once with the library's launch trace on; (kernel, ms) list."""
+    lib = esa._lib.load()
+    torch.cuda.synchronize()
+    lib.esa_trace_enable(1)
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        lib.esa_trace_enable(0)
+    return esa._lib.trace_records()
+
+
+def gather_probes(esa, q, k, v, spec, reps=3):
+    """Row-gather ceilings on this problem (esa_probe_gather): the tile
+    kernels' exact row stream, uniformly random rows of a KV head (L2), random
+    rows within 64 per CTA (L1); GB/s of 256-byte rows (K and V)."""
+    import ctypes
+    lib = esa._lib.load()
+    sink = torch.zeros(4, dtype=torch.int32, device=q.device)
+    pb = esa.ops._problem(q, k, spec, D ** -0.5, None, 0, k.shape[2], 0)
+    units = B * q.shape[1] * q.shape[2] * spec.attention_length
+    nbytes = units * 2 * D * ES
+    stream = torch.cuda.current_stream()
+    out = {}
+    for mode, name in ((0, "pattern"), (1, "l2_random"), (2, "l1_window")):
+        def run():
+            esa._lib.check(lib.esa_probe_gather(mode, ctypes.byref(pb), esa._lib.tensor4(k),
+                                                esa._lib.tensor4(v), sink.data_ptr(),
+                                                stream.cuda_stream), "esa_probe_gather")
+        run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        out[name] = {"ms": round(ms, 3), "GBps": round(nbytes / (ms * 1e-3) / 1e9, 1)}
+    out["rows_per_launch"] = 2 * units
+    out["row_bytes"] = D * ES
+    return out
+
+
+def timed_steps(step, steps, warmup, dev, world, clocks_gpu=None):
+    """Device ms per step over `steps` steps after `warmup`, max over ranks,
+    and the clock summary sampled during the timed region."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if clocks_gpu is None else clocks_gpu) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, dev, world)
+    if world > 1:
+        torch.distributed.barrier()
+    return ms, clocks.summary()
+
+
+def bench_ours(args, world, rank, local):
+    import elastic_sparse_attention_b200 as esa
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    hbm_peak, tc_peak, peak_src = peaks()
+    h0, nh, kv0, nkv = esa.head_share(HQ, HKV, rank, world)
+    q, k, v, do = make_inputs(dev, 1234, (h0, h0 + nh), (kv0, kv0 + nkv))
+    scale = D ** -0.5
+    specs = [esa.PatternSpec(layer, NL, W).heads(HQ, h0) for layer in range(NL)]
+    ws = torch.empty(esa.ops.backward_workspace_bytes(q, k, specs[0]), dtype=torch.uint8,
+                     device=dev)
+    for layer in range(NL):   # one-time pattern audit (backward precondition), outside timing
+        assert esa.ops.pattern_audit(HQ, esa.PatternSpec(layer, NL, W), L, dev) == 0
+    probs = [esa.ops.probs_buffer(q, k, s) for s in specs]
+
+    def step():
+        for s, pr in zip(specs, probs):
+            o, lse = esa.ops.forward(q, k, v, s, scale, probs=pr)
+            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws, probs=pr)
+
+    ms, clocks = timed_steps(step, args.steps, args.warmup, dev, world)
+
+    # Per-layer and per-family device times: one traced step (events around
+    # every library launch, on the launching stream).
+    recs = trace_step(esa, step)
+    launches_per_step = len(recs)
+    per_layer, fam_ms, fam_n = [], {}, {}
+    li = 0
+    cur = {"layer": 0, "fwd_ms": 0.0, "bwd_ms": 0.0}
+    for name, t in recs:
+        fam = FAMILY.get(name, name)
+        fam_ms[fam] = fam_ms.get(fam, 0.0) + t
+        fam_n[fam] = fam_n.get(fam, 0) + 1
+        if fam.startswith("fwd") and cur["bwd_ms"] > 0:   # next layer starts
+            per_layer.append(cur)
+            li += 1
+            cur = {"layer": li, "fwd_ms": 0.0, "bwd_ms": 0.0}
+        cur["fwd_ms" if fam.startswith("fwd") else "bwd_ms"] += t
+    per_layer.append(cur)
+    for p in per_layer:
+        p["fwd_ms"], p["bwd_ms"] = round(p["fwd_ms"], 3), round(p["bwd_ms"], 3)
+
+    fbytes = family_bytes(nh, nkv)
+    traffic = load_traffic()
+    families = {}
+    for fam, t in sorted(fam_ms.items(), key=lambda kv: -kv[1]):
+        n_layers = 1 if fam.endswith("window") else (NL - 1 if fam in fbytes else 0)
+        alg, impl = fbytes.get(fam, (0, 0))
+        d = {"launches": fam_n[fam], "ms_per_step": round(t, 3),
+             "share": round(t / sum(fam_ms.values()), 4)}
+        if alg and n_layers:
+            per_layer_ms = t / n_layers
+            d.update({"ms_per_layer": round(per_layer_ms, 3),
+                      "algorithmic_bytes_per_layer": alg,
+                      "implementation_bytes_per_layer": impl,
+                      "achieved_GBps": round(alg / (per_layer_ms * 1e-3) / 1e9, 1),
+                      "frac_of_hbm": round(alg / (per_layer_ms * 1e-3) / 1e9 / hbm_peak, 4)})
+            tr = traffic.get("families", {}).get(fam) if world == 1 else None
+            if tr:
+                d["traffic_bytes_per_layer"] = tr
+                d["traffic_over_algorithmic"] = round(tr / alg, 2)
+            if fam in ("fwd_tile", "bwd_query", "bwd_key"):
+                units = B * nh * L * W
+                d["gather_GBps"] = round(units * 2 * D * ES / (per_layer_ms * 1e-3) / 1e9, 1)
+        families[fam] = d
+    families["note"] = ("per GPU; algorithmic = the bytes the family's role must move "
+                        "(compulsory), implementation = this build's intermediates; traffic = "
+                        "measured DRAM bytes (profiles/traffic.json, 1 GPU)")
+
+    if rank == 0:
+        blocks = active_blocks_and_pairs(esa, dev)
+        if [a for a, _ in blocks] != ACTIVE_BLOCKS_C3 or [p for _, p in blocks] != VALID_PAIRS_C3:
+            raise RuntimeError(f"device pattern block counts {blocks} disagree with the oracle table")
+    eff_flop = sum(3.5 * 4 * D * TILE * TILE * a for a in ACTIVE_BLOCKS_C3) * B
+    useful_flop = sum(14 * D * p for p in VALID_PAIRS_C3) * B
+    value = eff_flop / (ms * 1e-3) / 1e12
+    useful = useful_flop / (ms * 1e-3) / 1e12
+
+    # Roofline: the backward of a dilated layer (the dominant family, all its
+    # launches) on compulsory HBM bytes; the gather ceiling it is really held by.
+    fwd_b, bwd_b = layer_bytes(nh, nkv)
+    dil = [p for p in per_layer if p["layer"] > 0]
+    bwd_ms = statistics.mean(p["bwd_ms"] for p in dil)
+    fwd_ms = statistics.mean(p["fwd_ms"] for p in dil)
+    achieved = bwd_b / (bwd_ms * 1e-3) / 1e9
+    probes = gather_probes(esa, q, k, v, specs[5])
+    gather_bwd = 2 * B * nh * L * W * 2 * D * ES / (bwd_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "backward of a dilated layer (query side + key side, "
+                                          "all launches), mean of layers 1-7",
+                "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4),
+                "traffic": traffic.get("bwd") if world == 1 else None,
+                "algorithmic_bytes": bwd_b,
+                "traffic_over_algorithmic": (round(traffic["bwd"] / bwd_b, 2)
+                                             if traffic.get("bwd") and world == 1 else None),
+                "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs)",
+                "ms_per_launch_set": round(bwd_ms, 3),
+                "gather": {"bytes_per_unit": 2 * 2 * D * ES,
+                           "achieved_GBps": round(gather_bwd, 1),
+                           "pattern_probe_GBps": probes["pattern"]["GBps"],
+                           "frac_of_pattern_probe": round(gather_bwd / probes["pattern"]["GBps"], 4),
+                           "note": "the backward moves 4 rows of 256 B per (query, head, slot); "
+                                   "the probe moves the tile kernels' 2 rows per unit with no "
+                                   "arithmetic"},
+                "forward": {"ms_per_layer": round(fwd_ms, 3), "algorithmic_bytes": fwd_b,
+                            "frac": round(fwd_b / (fwd_ms * 1e-3) / 1e9 / hbm_peak, 4)}}
+
+    e2e = e2e_module(esa, args, dev, world, rank, (h0, nh, kv0, nkv))
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic N(0,1), seeded",
+        "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": L,
+                   "heads": f"{HQ}q/{HKV}kv", "head_dim": D, "attention_length": W,
+                   "num_hidden_layers": NL,
+                   "parallelism": (f"head split x{world}: {nkv} KV heads ({nh} query heads) per "
+                                   "rank, no collective" if world > 1 else "1 GPU"),
+                   "l2": "inputs 2.7 GB > 126 MB L2, no flush"},
+        "value_note": "dense-equivalent count over touched 128x128 blocks (the north-star "
+                      "definition); can exceed the dense peak; see useful_tflops",
+        "useful_tflops": round(useful, 2),
+        "useful_frac_of_bf16_peak": round(useful / tc_peak, 5),
+        "effective_frac_of_bf16_peak": round(value / world / tc_peak, 4),
+        "kernel_ms_per_step": {"fwd": round(sum(p["fwd_ms"] for p in per_layer), 3),
+                               "bwd": round(sum(p["bwd_ms"] for p in per_layer), 3)},
+        "per_layer": per_layer,
+        "families": families,
+        "gather_peaks": probes,
+        "roofline": roofline,
+        "gpu_launches": args.steps * launches_per_step,
+        "clocks": clocks,
+        "e2e": e2e,
+    }
+    del probs, ws
+    torch.cuda.empty_cache()
+    return line, (q, k, v, do, specs)
+
+
+def e2e_module(esa, args, dev, world, rank, share):
+    """The same step through the public module (ElasticSparseAttention, or
+    HeadShardedElasticSparseAttention for this rank's heads) + autograd, with
+    q/k/v/dO copied from pinned host memory every step and dq/dk/dv read back
+    to pinned host memory every step.  The copies run on their own streams,
+    pipelined like a training loop with a prefetching loader: the inputs of
+    step s+1 are copied while step s computes (two device input buffers), and
+    the gradients of step s are read back while step s+1 computes.  The timed
+    region covers the first step's input copy through the last step's
+    read-back."""
+    h0, nh, kv0, nkv = share
+    g = torch.Generator().manual_seed(99)
+    host_in = {"q": torch.randn(B, nh, L, D, generator=g),
+               "k": torch.randn(B, nkv, L, D, generator=g),
+               "v": torch.randn(B, nkv, L, D, generator=g),
+               "do": torch.randn(B, L, nh * D, generator=g)}
+    host_in = {n: t.to(torch.bfloat16).pin_memory() for n, t in host_in.items()}
+    host_out = [torch.empty(B, nh, L, D, dtype=torch.bfloat16).pin_memory(),
+                torch.empty(B, nkv, L, D, dtype=torch.bfloat16).pin_memory(),
+                torch.empty(B, nkv, L, D, dtype=torch.bfloat16).pin_memory()]
+    dev_in = [{n: torch.empty_like(t, device=dev) for n, t in host_in.items()} for _ in range(2)]
+    if world == 1:
+        mods = [esa.ElasticSparseAttention(layer, NL, HQ, D, W, L, num_key_value_heads=HKV)
+                for layer in range(NL)]
+        call = lambda m, q, k, v: m(q, k, v)[0]
+    else:
+        mods = [esa.HeadShardedElasticSparseAttention(layer, NL, HQ, D, W, L,
+                                                      num_key_value_heads=HKV, rank=rank,
+                                                      world_size=world)
+                for layer in range(NL)]
+        call = lambda m, q, k, v: m(q, k, v)
+    compute = torch.cuda.current_stream(dev)
+    h2d_stream = torch.cuda.Stream(dev)
+    d2h_stream = torch.cuda.Stream(dev)
+    freed = [None, None]   # event: compute finished reading input buffer i
+
+    def h2d(i):
+        with torch.cuda.stream(h2d_stream):
+            if freed[i] is not None:
+                h2d_stream.wait_event(freed[i])
+            for n, t in host_in.items():
+                dev_in[i][n].copy_(t, non_blocking=True)
+            return h2d_stream.record_event()
+
+    def step(i, ready):
+        compute.wait_event(ready)
+        buf = dev_in[i]
+        q, k, v = (buf[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
+        for m in mods:
+            call(m, q, k, v).backward(buf["do"])
+        freed[i] = compute.record_event()
+        grads = (q.grad, k.grad, v.grad)
+        with torch.cuda.stream(d2h_stream):
+            d2h_stream.wait_event(freed[i])
+            for h, t in zip(host_out, grads):
+                h.copy_(t, non_blocking=True)
+                t.record_stream(d2h_stream)
+
+    def run(n):
+        ready = h2d(0)
+        for s_ in range(n):
+            nxt = h2d((s_ + 1) % 2) if s_ + 1 < n else None
+            step(s_ % 2, ready)
+            ready = nxt
+        compute.wait_stream(d2h_stream)
+
+    run(max(1, min(args.warmup, 2)))
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    n = max(10, args.steps)   # enough steps that the pipeline's fill and drain amortise
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(compute)
+    h2d_stream.wait_event(e0)
+    run(n)
+    e1.record(compute)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n, dev, world)
+    h2d_bytes = sum(t.numel() * t.element_size() for t in host_in.values()) * world
+    d2h_bytes = sum(t.numel() * t.element_size() for t in host_out) * world
+    eff = sum(3.5 * 4 * D * TILE * TILE * a for a in ACTIVE_BLOCKS_C3) * B
+    return {"value": round(eff / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 3), "h2d_bytes_per_step": h2d_bytes,
+            "d2h_bytes_per_step": d2h_bytes, "steps": n,
+            "api": "ElasticSparseAttention" if world == 1 else "HeadShardedElasticSparseAttention",
+            "pipelining": "inputs of step s+1 copied during step s; gradients of step s read "
+                          "back during step s+1; separate copy streams"}
+
+
+def bench_weak(esa, args, dev, world):
+    """Weak scaling: every rank runs the whole C3 problem (a batch split)."""
+    q, k, v, do = make_inputs(dev, 77)
+    scale = D ** -0.5
+    specs = [esa.PatternSpec(layer, NL, W) for layer in range(NL)]
+    ws = torch.empty(esa.ops.backward_workspace_bytes(q, k, specs[0]), dtype=torch.uint8,
+                     device=dev)
+    probs = [esa.ops.probs_buffer(q, k, s) for s in specs]
+
+    def step():
+        for s, pr in zip(specs, probs):
+            o, lse = esa.ops.forward(q, k, v, s, scale, probs=pr)
+            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws, probs=pr)
+
+    ms, _ = timed_steps(step, 3, 2, dev, world)
+    eff = sum(3.5 * 4 * D * TILE * TILE * a for a in ACTIVE_BLOCKS_C3) * B
+    del q, k, v, do, ws, probs
+    torch.cuda.empty_cache()
+    return {"value": round(eff * world / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 3), "global_batch": world, "steps": 3,
+            "parallelism": f"batch split x{world}: the whole C3 problem on every rank"}
+
+
+def bench_c2(esa, dev):
+    """C2: forward only, B=2, 32 heads, L=32768, D=128, bf16, q/k/v ~
+    N(0,1) * D^-0.25; per layer through the ops and through the module."""
+    hbm_peak, _, _ = peaks()
+    g = torch.Generator(device=dev).manual_seed(2)
+    s = D ** -0.25
+    q, k, v = (torch.randn(C2_B, C2_H, C2_L, D, device=dev, generator=g).mul_(s)
+               .to(torch.bfloat16) for _ in range(3))
+    stream = torch.cuda.current_stream()
+    per_layer, total = [], 0.0
+    comp = 2 * 2 * C2_B * C2_H * C2_L * D * ES + C2_B * C2_H * C2_L * 4
+    for layer in range(NL):
+        m = esa.ElasticSparseAttention(layer, NL, C2_H, D, W, C2_L).eval()
+        with torch.no_grad():
+            for _ in range(2):
+                m(q, k, v)
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            e[0].record(stream)
+            reps = 5
+            for _ in range(reps):
+                m(q, k, v)
+            e[1].record(stream)
+            torch.cuda.synchronize()
+        t = e[0].elapsed_time(e[1]) / reps
+        total += t
+        per_layer.append({"layer": layer, "ms": round(t, 3),
+                          "frac_of_hbm": round(comp / (t * 1e-3) / 1e9 / hbm_peak, 4)})
+    units = C2_B * C2_H * C2_L * W * NL
+    del q, k, v
+    torch.cuda.empty_cache()
+    return {"workload": "C2: forward of the 8 P8 layers, B=2, 32 heads, L=32768, D=128, bf16, "
+                        "N(0,1)*D^-0.25, through ElasticSparseAttention (no_grad)",
+            "ms_per_8_layers": round(total, 3), "per_layer": per_layer,
+            "useful_tflops": round(4 * D * units / (total * 1e-3) / 1e12, 2),
+            "compulsory_bytes_per_layer": comp}
+
+
+def module_layer_times(esa, q, k, v, do):
+    """Per layer, device ms of our drop-in module's forward and backward (the
+    calls the reference's module makes: forward with the output reshape, then
+    autograd backward), for the comparison with the reference's Triton path."""
+    stream = torch.cuda.current_stream()
+    do_hf = do.transpose(1, 2).reshape(B, L, HQ * D)
+    out = []
+    for layer in range(NL):
+        m = esa.ElasticSparseAttention(layer, NL, HQ, D, W, L, num_key_value_heads=HKV)
+        qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+        o, _ = m(qq, kk, vv)
+        o.backward(do_hf)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        qq.grad = kk.grad = vv.grad = None
+        ev[0].record(stream)
+        o, _ = m(qq, kk, vv)
+        ev[1].record(stream)
+        o.backward(do_hf)
+        ev[2].record(stream)
+        torch.cuda.synchronize()
+        out.append({"layer": layer, "fwd_ms": round(ev[0].elapsed_time(ev[1]), 3),
+                    "bwd_ms": round(ev[1].elapsed_time(ev[2]), 3)})
+        if layer == NL - 1:
+            sample = o.detach()[0, L - 1].float().cpu()
+        del o, qq, kk, vv
+    torch.cuda.empty_cache()
+    return out, sample
+
+
+def gpu_incumbent(args, ours_layers, our_sample):
+    """The reference's own Triton path (unmodified module from baseline/_ref)
+    timed on this GPU in a subprocess with a time limit; per layer, its
+    module-level forward / backward device time next to ours."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.exists(os.path.join(ref_dir, "elastic_sparse_attention.py")):
+        return {"unavailable": "baseline/_ref (the reference install) is absent"}
+    fd, path = tempfile.mkstemp(suffix=".json")
+    os.close(fd)
+    cmd = [sys.executable, os.path.abspath(__file__), "--incumbent-worker", path]
+    t0 = time.time()
+    try:
+        proc = subprocess.run(cmd, capture_output=True, text=True, timeout=args.incumbent_timeout)
+        status = f"exit {proc.returncode}"
+        tail = (proc.stderr or "")[-1500:]
+    except subprocess.TimeoutExpired:
+        status, tail = f"killed after {args.incumbent_timeout} s (partial results kept)", ""
+    res = {}
+    try:
+        with open(path) as f:
+            res = json.load(f)
+    except Exception:
+        pass
+    os.unlink(path)
+    res["status"] = status
+    res["wall_s"] = round(time.time() - t0, 1)
+    if tail and status != "exit 0":
+        res["stderr_tail"] = tail
+    ratios = []
+    for r in res.get("c3", []):
+        ours = next((o for o in ours_layers if o["layer"] == r["layer"]), None)
+        if ours and "fwd_ms" in r:
+            r["ours_fwd_ms"] = ours["fwd_ms"]
+            r["fwd_speedup"] = round(r["fwd_ms"] / ours["fwd_ms"], 2)
+        if ours and "bwd_ms" in r:
+            r["ours_bwd_ms"] = ours["bwd_ms"]
+            r["bwd_speedup"] = round(r["bwd_ms"] / ours["bwd_ms"], 2)
+            ratios.append((r["fwd_ms"] + r["bwd_ms"]) / (ours["fwd_ms"] + ours["bwd_ms"]))
+    if "sample_l7" in res and our_sample is not None:
+        ref = torch.tensor(res.pop("sample_l7"))
+        res["check_l7_last_row_max_abs_diff"] = round(float((ref - our_sample).abs().max()), 5)
+    if ratios:
+        res["c3_step_speedup"] = round(sum(r["fwd_ms"] + r.get("bwd_ms", 0) for r in res["c3"]) /
+                                       sum(o["fwd_ms"] + o["bwd_ms"] for o in ours_layers
+                                           if any(r["layer"] == o["layer"] for r in res["c3"])), 2)
+    return res
+
+
+def incumbent_worker(path):
+    """Runs in its own process: the reference's unmodified ElasticSparseAttention
+    (implementation="triton", its default) from baseline/_ref, nothing of this
+    repository's package; C3 forward + backward per layer, then C2 forward per
+    layer.  Results are written to `path` after every layer."""
+    sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+    import elastic_sparse_attention as ref_mod
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream()
+    res = {"module": "elastic_sparse_attention.ElasticSparseAttention (implementation='triton') "
+                     "from baseline/_ref, unmodified",
+           "timing": "device ms (CUDA events) of one module forward and one autograd backward, "
+                     "after a warm-up call (Triton JIT + autotune)", "c3": [], "c2": []}
+
+    def save():
+        with open(path, "w") as f:
+            json.dump(res, f)
+
+    def ev():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        return e
+
+    try:
+        q, k, v, do = make_inputs(dev, 1234)
+        do_hf = do.transpose(1, 2).reshape(B, L, HQ * D)
+        for layer in range(NL):
+            t0 = time.time()
+            m = ref_mod.ElasticSparseAttention(layer, NL, HQ, D, W, L,
+                                               num_key_value_heads=HKV).to(dev)
+            rec = {"layer": layer, "module_build_s": round(time.time() - t0, 1)}
+            qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+            out, _ = m(qq, kk, vv)          # warm-up: compile + autotune (forward)
+            torch.cuda.synchronize()
+            a = ev()
+            out, _ = m(qq, kk, vv)
+            b_ = ev()
+            torch.cuda.synchronize()
+            rec["fwd_ms"] = round(a.elapsed_time(b_), 3)
+            if layer == NL - 1:
+                res["sample_l7"] = out.detach()[0, L - 1].float().cpu().tolist()
+            res["c3"].append(rec)
+            save()
+            try:
+                out.backward(do_hf)            # warm-up: compile + autotune (backward)
+                torch.cuda.synchronize()
+                out, _ = m(qq, kk, vv)
+                torch.cuda.synchronize()
+                a = ev()
+                out.backward(do_hf)
+                b_ = ev()
+                torch.cuda.synchronize()
+                rec["bwd_ms"] = round(a.elapsed_time(b_), 3)
+            except Exception as exc:           # record the failure verbatim
+                rec["bwd_error"] = f"{type(exc).__name__}: {exc}"[:800]
+            save()
+            del m, out, qq, kk, vv
+            torch.cuda.empty_cache()
+        del q, k, v, do, do_hf
+        torch.cuda.empty_cache()
+        g = torch.Generator(device=dev).manual_seed(2)
+        s = D ** -0.25
+        q, k, v = (torch.randn(C2_B, C2_H, C2_L, D, device=dev, generator=g).mul_(s)
+                   .to(torch.bfloat16) for _ in range(3))
+        for layer in range(NL):
+            m = ref_mod.ElasticSparseAttention(layer, NL, C2_H, D, W, C2_L).to(dev)
+            with torch.no_grad():
+                m(q, k, v)
+                torch.cuda.synchronize()
+                a = ev()
+                m(q, k, v)
+                b_ = ev()
+                torch.cuda.synchronize()
+            res["c2"].append({"layer": layer, "fwd_ms": round(a.elapsed_time(b_), 3)})
+            save()
+            del m
+    except Exception as exc:
+        res["error"] = f"{type(exc).__name__}: {exc}"[:800]
+    save()
+
+
+def bench_c5(args, world, rank, local, steps=3, warmup=2):
+    """C5: B=1, 16 heads, D=128, L=2^20, bf16, the 8 P8 layers fwd+bwd, query
+    rows (and K/V rows) split across the ranks; each rank fetches the remote
+    K/V range its queries read over NCCL and returns partial dK/dV (strong
+    scaling: the total work is fixed).  Also per rank: device time in the
+    exchanges versus the kernels."""
+    import elastic_sparse_attention_b200 as esa
+    if not torch.distributed.is_initialized():
+        import datetime
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        torch.distributed.init_process_group("nccl", rank=0, world_size=1,
+                                             timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    S = C5_L // world
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    q = torch.randn(B, S, C5_H, D, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, S, C5_H, D, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, S, C5_H, D, device=dev, generator=g).to(torch.bfloat16)
+    do = torch.randn(B, S, C5_H * D, device=dev, generator=g).to(torch.bfloat16)
+    mods = [esa.SequenceShardedElasticSparseAttention(layer, NL, C5_H, D, W, C5_L)
+            for layer in range(NL)]
+    fetched = 0   # largest number of remote K/V rows any rank fetches for one layer
+    for m in mods:
+        plan = m.plan(S, dev)
+        fetched = max([fetched] + [sum(b - a for (_, a, b) in plan.pieces_needed(r))
+                                   for r in range(world)])
+
+    def step():
+        qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+        for m in mods:
+            out = m(qq, kk, vv)
+            out.backward(do)
+
+    ms, clocks = timed_steps(step, steps, warmup, dev, world)
+    prof = esa.sharded.profile_step(step, dev)
+    prof_all = [prof]
+    if world > 1:
+        prof_all = [None] * world
+        torch.distributed.all_gather_object(prof_all, prof)
+    useful = 14 * D * C5_H * C5_L * W * NL / (ms * 1e-3) / 1e12
+    del q, k, v, do, mods
+    torch.cuda.empty_cache()
+    return {"metric": "useful TFLOP/s, fwd+bwd, 1M ctx, sequence-sharded (C5)",
+            "value": round(useful, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": round(ms, 3), "scaling": "strong",
+            "workload": "C5: fwd+bwd of the 8 P8 layers, B=1, 16 heads, L=2^20, D=128, bf16, "
+                        "query rows split over the ranks, remote K/V fetched with NCCL",
+            "rows_per_rank": S, "max_rows_fetched_per_layer_per_rank": fetched,
+            "per_rank_ms": prof_all, "clocks": clocks}
 
 
 def cpu_baseline_sample(target_s: float, layer: int = NL - 1, threads: int | None = None):
@@ -208,222 +846,6 @@ def cpu_baseline_sample(target_s: float, layer: int = NL - 1, threads: int | Non
     return NL * (fixed + slope * L), r_b, nthreads
 
 
-def bench_ours(args, world, rank, local):
-    import elastic_sparse_attention_b200 as esa
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    hbm_peak, tc_peak, peak_src = peaks()
-    q, k, v, do = make_inputs(dev, seed=1234 + rank)
-    scale = D ** -0.5
-    specs = [esa.PatternSpec(layer, NL, W) for layer in range(NL)]
-    ws = torch.empty(esa.ops.backward_workspace_bytes(q, k, specs[0]), dtype=torch.uint8, device=dev)
-    for s in specs:   # one-time pattern audit (backward precondition), outside timing
-        assert esa.ops.pattern_audit(HQ, s, L, dev) == 0
-
-    probs = [esa.ops.probs_buffer(q, k, s) for s in specs]
-
-    def step():
-        for s, pr in zip(specs, probs):
-            o, lse = esa.ops.forward(q, k, v, s, scale, probs=pr)
-            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws, probs=pr)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(args.steps):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-        torch.distributed.barrier()
-
-    # Per-kernel breakdown (separate pass, events on the launching stream).
-    per_layer = []
-    kern = {"fwd": 0.0, "bwd": 0.0}
-    for s in specs:
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-        reps = 2
-        ev[0].record(stream)
-        pr = probs[s.layer_idx]
-        for _ in range(reps):
-            o, lse = esa.ops.forward(q, k, v, s, scale, probs=pr)
-        ev[1].record(stream)
-        for _ in range(reps):
-            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws, probs=pr)
-        ev[2].record(stream)
-        torch.cuda.synchronize()
-        f_ms, b_ms = ev[0].elapsed_time(ev[1]) / reps, ev[1].elapsed_time(ev[2]) / reps
-        per_layer.append({"layer": s.layer_idx, "fwd_ms": round(f_ms, 3), "bwd_ms": round(b_ms, 3)})
-        kern["fwd"] += f_ms
-        kern["bwd"] += b_ms
-
-    blocks = active_blocks_and_pairs(esa, dev)
-    if [a for a, _ in blocks] != ACTIVE_BLOCKS_C3 or [p for _, p in blocks] != VALID_PAIRS_C3:
-        raise RuntimeError(f"device pattern block counts {blocks} disagree with the oracle table")
-    eff_flop = sum(3.5 * 4 * D * TILE * TILE * a for a, _ in blocks) * B
-    useful_flop = sum(14 * D * p for _, p in blocks) * B
-    value = eff_flop * world / (ms * 1e-3) / 1e12
-    useful = useful_flop * world / (ms * 1e-3) / 1e12
-
-    # Roofline of the dominant kernel family (backward): compulsory HBM bytes
-    # per launch set over its measured time.
-    es = 2
-    q_b, kv_b = B * HQ * L * D * es, B * HKV * L * D * es
-    pairs_total = sum(p for _, p in blocks) / NL
-    bwd_bytes = (3 * q_b + 2 * kv_b + B * HQ * L * 4   # read q, o, dO, k, v, lse
-                 + q_b + 2 * kv_b                      # write dq, dk, dv
-                 + 2 * B * HQ * W * L * 8              # (p, dS) workspace write + read
-                 + 2 * 2 * B * HKV * L * D * 4 * (HQ // HKV - 1))  # fp32 dK/dV accumulators
-    fwd_bytes = q_b + 2 * kv_b + q_b + B * HQ * L * 4
-    dom = "bwd" if kern["bwd"] >= kern["fwd"] else "fwd"
-    dom_ms = kern[dom] / NL
-    dom_bytes = bwd_bytes if dom == "bwd" else fwd_bytes
-    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tpath):
-        try:
-            traffic = json.load(open(tpath)).get(dom)
-        except Exception:
-            traffic = None
-    roofline = {"bound": "hbm", "kernel": f"{dom} (per layer, all launches)",
-                "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                "peak_source": peak_src,
-                "gather_GBps": round(2 * 2 * pairs_total * D * es * (2 if dom == "bwd" else 1)
-                                     / (dom_ms * 1e-3) / 1e9, 1),
-                "note": "algorithmic = compulsory HBM bytes; the gather kernels are bound by "
-                        "L1/L2->SM row-gather bandwidth (gather_GBps), not HBM"}
-
-    # End to end through the public module with pinned host buffers.
-    e2e = e2e_module(esa, args, dev, world)
-
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic N(0,1), seeded",
-        "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": L,
-                   "heads": f"{HQ}q/{HKV}kv", "head_dim": D, "attention_length": W,
-                   "num_hidden_layers": NL, "parallelism": f"batch split x{world}, no collective",
-                   "l2": "inputs 2.5 GB/GPU > 126 MB L2, no flush"},
-        "useful_tflops": round(useful, 2),
-        "useful_frac_of_bf16_peak": round(useful / tc_peak, 5),
-        "effective_frac_of_bf16_peak": round(value / world / tc_peak, 4),
-        "kernel_ms_per_step": {k2: round(v2, 3) for k2, v2 in kern.items()},
-        "per_layer": per_layer,
-        "active_blocks_per_layer": [a for a, _ in blocks],
-        "roofline": roofline,
-        # per step: layer 0 = window forward + 2 window backward kernels; layers
-        # 1..7 = tile forward + query-side tile backward + long-run chunk kernel
-        # + the key-side launches (KEY_HEADS_PER_LAUNCH query heads of a group each)
-        "gpu_launches": args.steps * (3 + (NL - 1) * (3 + -(-(HQ // HKV) // KEY_HEADS_PER_LAUNCH))),
-        "clocks": clocks.summary(),
-        "e2e": e2e,
-    }
-    if world == 1 and not args.no_cpu_baseline:
-        sec_step, rows, thr = cpu_baseline_sample(args.cpu_seconds)
-        line["cpu_baseline"] = {
-            "value": round(eff_flop / sec_step / 1e12, 6), "unit": UNIT, "cores": thr,
-            "kind": "port",
-            "sample": f"oracle port of the reference naive path (bf16, torch CPU), fwd+bwd, "
-                      f"layer {NL - 1}, last {rows} query rows x {HQ} heads, extrapolated "
-                      f"linearly to {L} rows x {NL} layers ({sec_step:.1f} s/step)"}
-    return line
-
-
-def e2e_module(esa, args, dev, world):
-    """The same step through ElasticSparseAttention + autograd, with q/k/v/dO
-    copied from pinned host memory every step and dq/dk/dv read back to pinned
-    host memory every step.  The copies run on their own streams, pipelined
-    like a training loop with a prefetching loader: the inputs of step s+1
-    are copied while step s computes (two device input buffers), and the
-    gradients of step s are read back while step s+1 computes.  The timed
-    region covers the first step's input copy through the last step's
-    read-back."""
-    g = torch.Generator().manual_seed(99)
-    host_in = {"q": torch.randn(B, HQ, L, D, generator=g),
-               "k": torch.randn(B, HKV, L, D, generator=g),
-               "v": torch.randn(B, HKV, L, D, generator=g),
-               "do": torch.randn(B, L, HQ * D, generator=g)}
-    host_in = {n: t.to(torch.bfloat16).pin_memory() for n, t in host_in.items()}
-    host_out = [torch.empty(B, HQ, L, D, dtype=torch.bfloat16).pin_memory(),
-                torch.empty(B, HKV, L, D, dtype=torch.bfloat16).pin_memory(),
-                torch.empty(B, HKV, L, D, dtype=torch.bfloat16).pin_memory()]
-    dev_in = [{n: torch.empty_like(t, device=dev) for n, t in host_in.items()} for _ in range(2)]
-    mods = [esa.ElasticSparseAttention(layer, NL, HQ, D, W, L, num_key_value_heads=HKV)
-            for layer in range(NL)]
-    compute = torch.cuda.current_stream(dev)
-    h2d_stream = torch.cuda.Stream(dev)
-    d2h_stream = torch.cuda.Stream(dev)
-    freed = [None, None]   # event: compute finished reading input buffer i
-
-    def h2d(i):
-        with torch.cuda.stream(h2d_stream):
-            if freed[i] is not None:
-                h2d_stream.wait_event(freed[i])
-            for n, t in host_in.items():
-                dev_in[i][n].copy_(t, non_blocking=True)
-            return h2d_stream.record_event()
-
-    def step(i, ready):
-        compute.wait_event(ready)
-        buf = dev_in[i]
-        q, k, v = (buf[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
-        for m in mods:
-            out, _ = m(q, k, v)
-            out.backward(buf["do"])
-        freed[i] = compute.record_event()
-        grads = (q.grad, k.grad, v.grad)
-        with torch.cuda.stream(d2h_stream):
-            d2h_stream.wait_event(freed[i])
-            for h, t in zip(host_out, grads):
-                h.copy_(t, non_blocking=True)
-                t.record_stream(d2h_stream)
-
-    def run(n):
-        ready = h2d(0)
-        for s_ in range(n):
-            nxt = h2d((s_ + 1) % 2) if s_ + 1 < n else None
-            step(s_ % 2, ready)
-            ready = nxt
-        compute.wait_stream(d2h_stream)
-
-    run(max(1, min(args.warmup, 2)))
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    n = max(10, args.steps)   # enough steps that the pipeline's fill and drain amortise
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(compute)
-    h2d_stream.wait_event(e0)
-    run(n)
-    e1.record(compute)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / n
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    h2d_bytes = sum(t.numel() * t.element_size() for t in host_in.values())
-    d2h_bytes = sum(t.numel() * t.element_size() for t in host_out)
-    return {"ms_per_step": round(ms, 3), "h2d_bytes_per_step": h2d_bytes,
-            "d2h_bytes_per_step": d2h_bytes, "unit": UNIT, "value": None, "steps": n,
-            "pipelining": "inputs of step s+1 copied during step s; gradients of step s read "
-                          "back during step s+1; separate copy streams"}
-
-
 def bench_reference(args, world, rank):
     """CPU reference arm: the reference naive path (oracle port) on host cores."""
     if rank != 0:
@@ -434,7 +856,7 @@ def bench_reference(args, world, rank):
     value = eff * B / sec_step / 1e12
     return {"metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec_step * 1e3, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic N(0,1), seeded", "impl": "reference",
             "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": L,
                        "parallelism": "host CPU, rank 0 only"},
@@ -443,70 +865,6 @@ def bench_reference(args, world, rank):
                                        "step, extrapolated linearly in rows and layers"},
             "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
-
-
-def bench_c5(args, world, rank, local):
-    """C5: B=1, 16 heads, D=128, L=2^20, bf16, the 8 P8 layers fwd+bwd, query
-    rows (and K/V rows) split across the ranks; each rank fetches the remote
-    K/V range its queries read over NCCL and returns partial dK/dV (strong
-    scaling: the total work is fixed)."""
-    import elastic_sparse_attention_b200 as esa
-    L5, H5 = 1 << 20, 16
-    if world == 1 and not torch.distributed.is_initialized():
-        import datetime
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", "29533")
-        torch.distributed.init_process_group("nccl", rank=0, world_size=1,
-                                             timeout=datetime.timedelta(seconds=300),
-                                             device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    S = L5 // world
-    g = torch.Generator(device=dev).manual_seed(5 + rank)
-    q = torch.randn(B, S, H5, D, device=dev, generator=g).to(torch.bfloat16)
-    k = torch.randn(B, S, H5, D, device=dev, generator=g).to(torch.bfloat16)
-    v = torch.randn(B, S, H5, D, device=dev, generator=g).to(torch.bfloat16)
-    do = torch.randn(B, S, H5 * D, device=dev, generator=g).to(torch.bfloat16)
-    mods = [esa.SequenceShardedElasticSparseAttention(layer, NL, H5, D, W, L5) for layer in range(NL)]
-    fetched = 0   # largest number of remote K/V rows any rank fetches for one layer
-    for m in mods:
-        plan = m.plan(S, dev)
-        fetched = max([fetched] + [sum(b - a for (_, a, b) in plan.pieces_needed(r))
-                                   for r in range(world)])
-
-    def step():
-        qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
-        for m in mods:
-            out = m(qq, kk, vv)
-            out.backward(do)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    torch.distributed.barrier()
-    s_ = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        e0.record(s_)
-        for _ in range(args.steps):
-            step()
-        e1.record(s_)
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], device=dev)
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms = float(t.item())
-    useful = 14 * D * H5 * L5 * W * NL / (ms * 1e-3) / 1e12
-    return {"metric": "useful TFLOP/s, fwd+bwd, 1M ctx, sequence-sharded (C5)",
-            "value": round(useful, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic N(0,1), seeded",
-            "config": {"workload": "C5: fwd+bwd of the 8 P8 layers, B=1, 16 heads, L=2^20, D=128, "
-                                   "query rows split over the ranks, remote K/V fetched with NCCL",
-                       "seq_len": L5, "rows_per_rank": S, "parallelism": f"sequence split x{world}",
-                       "max_rows_fetched_per_layer_per_rank": fetched,
-                       "allocator": os.environ.get("PYTORCH_CUDA_ALLOC_CONF", "default")},
-            "clocks": clocks.summary()}
 
 
 def bench_c4(args):
@@ -656,24 +1014,25 @@ def profile_case(args):
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     n = args.seq_len
-    q = torch.randn(B, HQ, n, D, device=dev, generator=g).to(torch.bfloat16)
-    k = torch.randn(B, HKV, n, D, device=dev, generator=g).to(torch.bfloat16)
-    v = torch.randn(B, HKV, n, D, device=dev, generator=g).to(torch.bfloat16)
-    do = torch.randn(B, HQ, n, D, device=dev, generator=g).to(torch.bfloat16)
+    hq, hkv = args.heads, max(1, args.heads // (HQ // HKV))
+    q = torch.randn(B, hq, n, D, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, hkv, n, D, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, hkv, n, D, device=dev, generator=g).to(torch.bfloat16)
+    do = torch.randn(B, hq, n, D, device=dev, generator=g).to(torch.bfloat16)
     spec = esa.PatternSpec(args.layer, NL, W)
     for _ in range(args.steps):
         pr = esa.ops.probs_buffer(q, k, spec)
         o, lse = esa.ops.forward(q, k, v, spec, D ** -0.5, probs=pr)
         esa.ops.backward(q, k, v, o, lse, do, spec, D ** -0.5, probs=pr)
     torch.cuda.synchronize()
-    print(json.dumps({"case": "one-layer", "seq_len": n, "layer": args.layer,
+    print(json.dumps({"case": "one-layer", "seq_len": n, "layer": args.layer, "heads": hq,
                       "out_mean_abs": float(o.float().abs().mean())}))
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--workload", choices=["c3", "c4", "c5", "decode"], default="c3",
-                    help="c5: the 1M-token sequence-sharded configuration; decode: "
+                    help="c5: the 1M-token sequence-sharded configuration alone; decode: "
                          "per-token latency against a 128k K/V cache")
     ap.add_argument("--decode-rows", type=int, default=1)
     ap.add_argument("--c4-seq-len", type=int, default=262144)
@@ -683,13 +1042,23 @@ def main():
                     help="one-layer: a single fwd+bwd at --seq-len/--layer, for profilers")
     ap.add_argument("--seq-len", type=int, default=32768)
     ap.add_argument("--layer", type=int, default=5)
+    ap.add_argument("--heads", type=int, default=HQ, help="one-layer: query heads (GQA 4:1)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpu-incumbent", action="store_true",
+                    help="skip timing the reference's Triton kernel")
+    ap.add_argument("--incumbent-timeout", type=float, default=420.0)
+    ap.add_argument("--no-extras", action="store_true",
+                    help="C3 line only (no C2, C5, weak-scaling, incumbent or CPU legs)")
+    ap.add_argument("--incumbent-worker", default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.incumbent_worker:
+        incumbent_worker(args.incumbent_worker)
+        return
     if args.case == "one-layer":
         profile_case(args)
         return
@@ -706,26 +1075,54 @@ def main():
     if args.workload == "c4":
         print(json.dumps(bench_c4(args)), flush=True)
         return
-    if args.workload == "c5":
-        # every layer's K/V buffer has a different row count; expandable
-        # segments keep the cached blocks from fragmenting the 180 GB
-        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+    # every C5 layer's K/V buffer has a different row count; expandable
+    # segments keep the cached blocks from fragmenting the 180 GB
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     world, rank, local = dist_init()
     if args.workload == "c5":
-        line = bench_c5(args, world, rank, local)
+        line = bench_c5(args, world, rank, local, steps=args.steps, warmup=args.warmup)
         if rank == 0:
             print(json.dumps(line), flush=True)
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
         return
-    line = bench_ours(args, world, rank, local)
+    import elastic_sparse_attention_b200 as esa
+    dev = torch.device("cuda", local)
+    line, tensors = bench_ours(args, world, rank, local)
+    if not args.no_extras:
+        if world == 1:
+            q, k, v, do, _ = tensors
+            ours_layers, sample = module_layer_times(esa, q, k, v, do)
+            del q, k, v, do, tensors
+            torch.cuda.empty_cache()
+            line["module_per_layer"] = ours_layers
+            if not args.no_gpu_incumbent:
+                line["gpu_incumbent"] = gpu_incumbent(args, ours_layers, sample)
+            line["c2"] = bench_c2(esa, dev)
+            inc = line.get("gpu_incumbent", {})
+            if inc.get("c2"):
+                for o, r in zip(line["c2"]["per_layer"], inc["c2"]):
+                    o["triton_ms"] = r["fwd_ms"]
+                    o["speedup_vs_triton"] = round(r["fwd_ms"] / o["ms"], 2)
+        else:
+            del tensors
+            torch.cuda.empty_cache()
+            line["weak"] = bench_weak(esa, args, dev, world)
+        line["c5"] = bench_c5(args, world, rank, local)
+        if world == 1 and not args.no_cpu_baseline:
+            sec_step, rows, thr = cpu_baseline_sample(args.cpu_seconds)
+            eff = sum(3.5 * 4 * D * TILE * TILE * a for a in ACTIVE_BLOCKS_C3) * B
+            line["cpu_baseline"] = {
+                "value": round(eff / sec_step / 1e12, 6), "unit": UNIT, "cores": thr,
+                "kind": "port",
+                "sample": f"oracle port of the reference naive path (bf16, torch CPU), fwd+bwd, "
+                          f"layer {NL - 1}, last {rows} query rows x {HQ} heads, extrapolated "
+                          f"linearly to {L} rows x {NL} layers ({sec_step:.1f} s/step)"}
     if rank == 0:
-        eff_per_step = line["value"] * line["ms_per_step"] * 1e-3 * 1e12
-        e2e = line["e2e"]
-        e2e["value"] = round(eff_per_step / (e2e["ms_per_step"] * 1e-3) / 1e12, 2)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
+    if torch.distributed.is_initialized():
         torch.distributed.destroy_process_group()
 
 

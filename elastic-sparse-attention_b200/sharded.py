@@ -9,18 +9,27 @@ positions (the property the backward relies on; audited by
 smallest valid index of its first row, and every row above it up to r*S is
 read by some head and slot.
 
-Forward:  fetch rows [lo_r, r*S) of K and V from their owners (NCCL grouped
-          send/recv into one [rows, B, Hkv, D] buffer that also holds the
-          local rows), then run the forward with row_offset = r*S and
-          kv_offset = lo_r (the C ABI's offsets; indices are clamped to the
-          global length as the reference does).
-Backward: the local backward yields dQ for the local rows and partial dK/dV
-          for every row of the buffer; the partials for remote rows go back to
-          their owners (the reverse exchange) and are summed in fp32.
+The KV heads are processed in head groups (whole GQA groups), so that the
+transfers of one group overlap the kernels of the previous one:
 
-No reference counterpart: the reference runs on one device.  The layout of
-the local shards is sequence-major, [B, S, H, D] (what an HF-style attention
-layer produces), read in place by the kernels through strides.
+Forward:  for every head group, one grouped batch of NCCL send/recv fetches
+          rows [lo_r, r*S) of its K and V from their owners into a per-group
+          [rows, heads, D] buffer that also holds the local rows; all batches
+          are issued at once on the communicator's stream, and the compute
+          stream waits for group g's batch just before group g's forward
+          (row_offset = r*S, kv_offset = lo_r: the C ABI's offsets; indices
+          are clamped to the global length as the reference does).
+Backward: group g's backward yields dQ for the local rows and partial dK/dV
+          for every buffer row; the partials of remote rows go back to their
+          owners in one batch per group, issued right after that group's
+          kernels, so they travel while the next group computes; the owners
+          add them to their local partials in fp32.
+
+The NCCL traffic of a rank is the remote K/V rows its queries read (at most
+all rows below its shard, at alpha = 1) and the same rows of partial dK/dV
+back.  No reference counterpart: the reference runs on one device.  The layout
+of the local shards is sequence-major, [B, S, H, D] (what an HF-style
+attention layer produces), read in place by the kernels through strides.
 """
 from __future__ import annotations
 
@@ -86,100 +95,189 @@ def make_plan(num_heads: int, spec: PatternSpec, rows_per_rank: int, world: int,
     return plan
 
 
-def _exchange(plan: ShardPlan, rank: int, group, local: torch.Tensor, buf: torch.Tensor,
-              lo: int):
-    """Fill buf ([rows, ...], row 0 = position lo) with the remote rows rank
-    `rank` reads, and send the rows of `local` ([S, ...]) that higher ranks
-    read.  One grouped batch of NCCL / gloo point-to-point operations."""
+# ---------------------------------------------------------------------------
+# Optional per-step timing of one rank (profile_step): CUDA events on the
+# compute stream around the kernels and around each wait for a transfer.
+# ---------------------------------------------------------------------------
+_timing = threading.local()
+
+
+class _Span:
+    def __init__(self, kind: str):
+        self.kind = kind
+        self.rec = getattr(_timing, "records", None)
+
+    def __enter__(self):
+        if self.rec is not None:
+            self.a = torch.cuda.Event(enable_timing=True)
+            self.a.record()
+        return self
+
+    def __exit__(self, *exc):
+        if self.rec is not None:
+            b = torch.cuda.Event(enable_timing=True)
+            b.record()
+            self.rec.append((self.kind, self.a, b))
+
+
+def profile_step(step, device) -> dict:
+    """Runs step() once and splits this rank's device time (compute stream)
+    into kernels, waits for NCCL transfers, and the rest (layout copies,
+    fp32 sums, allocation); milliseconds."""
+    torch.cuda.synchronize(device)
+    _timing.records = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize(device)
+        recs = _timing.records
+    finally:
+        _timing.records = None
+    total = e0.elapsed_time(e1)
+    out = {"step_ms": round(total, 3)}
+    for kind in ("kernels", "exchange_wait"):
+        out[kind + "_ms"] = round(sum(a.elapsed_time(b) for k, a, b in recs if k == kind), 3)
+    out["other_ms"] = round(total - out["kernels_ms"] - out["exchange_wait_ms"], 3)
+    return out
+
+
+def _batch(p2p):
+    """Issue one grouped batch of point-to-point operations; [] if none."""
+    return dist.batch_isend_irecv(p2p) if p2p else []
+
+
+def _wait(works):
+    with _Span("exchange_wait"):
+        for w in works:
+            w.wait()
+
+
+def _fetch(plan: ShardPlan, rank: int, group, bufs, lo: int):
+    """Issue (do not wait for) the fetch of the remote rows of every buffer in
+    bufs ([rows, ...], row 0 = position lo, the local rows already in place)
+    and the sends of this rank's rows that higher ranks read (taken from the
+    local part of the same buffers).  Peers are ranks of `group`."""
     a0, _ = plan.owned(rank)
     p2p = []
-    for (q, a, b) in plan.pieces_needed(rank):
-        p2p.append(dist.P2POp(dist.irecv, buf[a - lo:b - lo], group=group, group_peer=q))
-    sends = []
-    for (r, a, b) in plan.pieces_sent(rank):
-        piece = local[a - a0:b - a0].contiguous()
-        sends.append(piece)
-        p2p.append(dist.P2POp(dist.isend, piece, group=group, group_peer=r))
-    if p2p:
-        for req in dist.batch_isend_irecv(p2p):
-            req.wait()
+    for buf in bufs:
+        for (q, a, b) in plan.pieces_needed(rank):
+            p2p.append(dist.P2POp(dist.irecv, buf[a - lo:b - lo], group=group, group_peer=q))
+        for (r, a, b) in plan.pieces_sent(rank):
+            p2p.append(dist.P2POp(dist.isend, buf[a - lo:b - lo], group=group, group_peer=r))
+    return _batch(p2p)
 
 
-def _reverse_exchange(plan: ShardPlan, rank: int, group, dbuf: torch.Tensor, lo: int,
-                      acc: torch.Tensor):
-    """Send the partial gradients of remote rows (dbuf rows below r*S) to their
-    owners; receive the partials of the local rows from higher ranks and add
-    them into acc ([S, ...], fp32)."""
-    a0, _ = plan.owned(rank)
+def _return_partials(plan: ShardPlan, rank: int, group, dbufs, lo: int):
+    """Issue the sends of the partial gradients of remote rows (rows below
+    r*S of each buffer in dbufs) to their owners and the receives of the
+    partials of this rank's rows from higher ranks; returns (works, [(buffer
+    index, tensor, start, stop)] of the receives)."""
     p2p, recvs = [], []
-    for (q, a, b) in plan.pieces_needed(rank):
-        p2p.append(dist.P2POp(dist.isend, dbuf[a - lo:b - lo].contiguous(), group=group,
-                                   group_peer=q))
-    for (r, a, b) in plan.pieces_sent(rank):
-        t = torch.empty((b - a,) + tuple(dbuf.shape[1:]), dtype=dbuf.dtype, device=dbuf.device)
-        recvs.append((t, a, b))
-        p2p.append(dist.P2POp(dist.irecv, t, group=group, group_peer=r))
-    if p2p:
-        for req in dist.batch_isend_irecv(p2p):
-            req.wait()
-    for (t, a, b) in recvs:
-        acc[a - a0:b - a0] += t.float()
+    for i, dbuf in enumerate(dbufs):
+        for (q, a, b) in plan.pieces_needed(rank):
+            p2p.append(dist.P2POp(dist.isend, dbuf[a - lo:b - lo], group=group, group_peer=q))
+        for (r, a, b) in plan.pieces_sent(rank):
+            t = torch.empty((b - a,) + tuple(dbuf.shape[1:]), dtype=dbuf.dtype,
+                            device=dbuf.device)
+            recvs.append((i, t, a, b))
+            p2p.append(dist.P2POp(dist.irecv, t, group=group, group_peer=r))
+    return _batch(p2p), recvs
+
+
+def group_count(num_kv_heads: int, wanted: int) -> int:
+    """Largest count <= wanted that divides num_kv_heads."""
+    n = max(1, min(wanted, num_kv_heads))
+    while num_kv_heads % n:
+        n -= 1
+    return n
 
 
 class _ShardedFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, spec: PatternSpec, scale: float, plan: ShardPlan, rank: int,
-                group, ops):
+                group, ops, ngroups: int):
         # q [B, S, Hq, D], k/v [B, S, Hkv, D] (sequence-major shards)
         B, S, Hq, D = q.shape
         Hkv = k.shape[2]
+        G = Hq // Hkv
+        hg = Hkv // ngroups                              # KV heads per head group
         a0, b0 = plan.owned(rank)
         lo = plan.lo[rank]
         rows = b0 - lo
         L = plan.world * plan.rows_per_rank
-        # [rows, B, Hkv, D]: row slices are contiguous for the exchange
-        kbuf = torch.empty((rows, B, Hkv, D), dtype=k.dtype, device=k.device)
+        # per head group: [rows, B, hg, D]; row slices are contiguous for the transfers
+        kbuf = torch.empty((ngroups, rows, B, hg, D), dtype=k.dtype, device=k.device)
         vbuf = torch.empty_like(kbuf)
-        kbuf[a0 - lo:] = k.transpose(0, 1)
-        vbuf[a0 - lo:] = v.transpose(0, 1)
-        _exchange(plan, rank, group, k.transpose(0, 1), kbuf, lo)
-        _exchange(plan, rank, group, v.transpose(0, 1), vbuf, lo)
-        qv = q.transpose(1, 2)                       # [B, Hq, S, D] view
-        kv_k = kbuf.permute(1, 2, 0, 3)              # [B, Hkv, rows, D] view
-        kv_v = vbuf.permute(1, 2, 0, 3)
-        probs = None
-        if hasattr(ops, "probs_buffer"):
-            # the forward leaves its probabilities for the backward (no score pass)
-            probs = ops.probs_buffer(qv, kv_k, spec, row_offset=a0, kv_len=L, kv_offset=lo)
-        o, lse = ops.forward(qv, kv_k, kv_v, spec, scale, row_offset=a0, kv_len=L, kv_offset=lo,
-                             **({"probs": probs} if probs is not None else {}))
-        ctx.save_for_backward(q, kbuf, vbuf, o, lse, probs)
-        ctx.meta = (spec, scale, plan, rank, group, ops)
-        return o.transpose(1, 2)                     # [B, S, Hq, D]
+        kbuf[:, a0 - lo:] = k.transpose(0, 1).reshape(S, B, ngroups, hg, D).permute(2, 0, 1, 3, 4)
+        vbuf[:, a0 - lo:] = v.transpose(0, 1).reshape(S, B, ngroups, hg, D).permute(2, 0, 1, 3, 4)
+        works = [_fetch(plan, rank, group, (kbuf[g], vbuf[g]), lo) for g in range(ngroups)]
+        out = torch.empty_like(q)                        # [B, S, Hq, D]
+        lses, probs = [], []
+        for g in range(ngroups):
+            h0 = g * hg * G
+            sg = spec.heads(Hq, h0)
+            qv = q[:, :, h0:h0 + hg * G].transpose(1, 2)  # [B, hg*G, S, D] view
+            kv_k = kbuf[g].permute(1, 2, 0, 3)              # [B, hg, rows, D] view
+            kv_v = vbuf[g].permute(1, 2, 0, 3)
+            pr = (ops.probs_buffer(qv, kv_k, sg, row_offset=a0, kv_len=L, kv_offset=lo)
+                  if hasattr(ops, "probs_buffer") else None)
+            _wait(works[g])
+            with _Span("kernels"):
+                _, lse = ops.forward(qv, kv_k, kv_v, sg, scale, row_offset=a0, kv_len=L,
+                                     kv_offset=lo, out=out[:, :, h0:h0 + hg * G].transpose(1, 2),
+                                     **({"probs": pr} if pr is not None else {}))
+            lses.append(lse)
+            probs.append(pr)
+        ctx.save_for_backward(q, kbuf, vbuf, out, *lses,
+                              *[p for p in probs if p is not None])
+        ctx.has_probs = [p is not None for p in probs]
+        ctx.meta = (spec, scale, plan, rank, group, ops, ngroups)
+        return out
 
     @staticmethod
     def backward(ctx, do):
         if do.stride(-1) != 1:
             do = do.contiguous()
-        q, kbuf, vbuf, o, lse, probs = ctx.saved_tensors
-        spec, scale, plan, rank, group, ops = ctx.meta
+        spec, scale, plan, rank, group, ops, ngroups = ctx.meta
+        saved = ctx.saved_tensors
+        q, kbuf, vbuf, out = saved[:4]
+        lses = saved[4:4 + ngroups]
+        it = iter(saved[4 + ngroups:])
+        probs = [next(it) if h else None for h in ctx.has_probs]
+        B, S, Hq, D = q.shape
+        hg = kbuf.shape[3]
+        G = Hq // (hg * ngroups)
         a0, _ = plan.owned(rank)
         lo = plan.lo[rank]
         L = plan.world * plan.rows_per_rank
-        dq, dkb, dvb = ops.backward(q.transpose(1, 2), kbuf.permute(1, 2, 0, 3),
-                                    vbuf.permute(1, 2, 0, 3), o, lse, do.transpose(1, 2), spec,
-                                    scale, row_offset=a0, kv_len=L, kv_offset=lo,
-                                    **({"probs": probs} if probs is not None else {}))
-        # partial dK/dV per buffer row, back in the [rows, B, Hkv, D] order
-        dk_rows = dkb.permute(2, 0, 1, 3)
-        dv_rows = dvb.permute(2, 0, 1, 3)
-        dk_acc = dk_rows[a0 - lo:].float()
-        dv_acc = dv_rows[a0 - lo:].float()
-        _reverse_exchange(plan, rank, group, dk_rows, lo, dk_acc)
-        _reverse_exchange(plan, rank, group, dv_rows, lo, dv_acc)
-        dk = dk_acc.to(kbuf.dtype).transpose(0, 1)   # [B, S, Hkv, D]
-        dv = dv_acc.to(vbuf.dtype).transpose(0, 1)
-        return dq.transpose(1, 2), dk, dv, None, None, None, None, None, None
+        dq = torch.empty_like(q)
+        dkb, dvb = torch.empty_like(kbuf), torch.empty_like(vbuf)
+        pending = []
+        for g in range(ngroups):
+            h0 = g * hg * G
+            sl = slice(h0, h0 + hg * G)
+            sg = spec.heads(Hq, h0)
+            with _Span("kernels"):
+                ops.backward(q[:, :, sl].transpose(1, 2), kbuf[g].permute(1, 2, 0, 3),
+                             vbuf[g].permute(1, 2, 0, 3), out[:, :, sl].transpose(1, 2), lses[g],
+                             do[:, :, sl].transpose(1, 2), sg, scale, row_offset=a0, kv_len=L,
+                             kv_offset=lo, dq=dq[:, :, sl].transpose(1, 2),
+                             dk=dkb[g].permute(1, 2, 0, 3), dv=dvb[g].permute(1, 2, 0, 3),
+                             **({"probs": probs[g]} if probs[g] is not None else {}))
+            pending.append(_return_partials(plan, rank, group, (dkb[g], dvb[g]), lo))
+        # local rows: own partials plus the partials returned by higher ranks, in fp32
+        dk_acc = dkb[:, a0 - lo:].float()                # [ngroups, S, B, hg, D]
+        dv_acc = dvb[:, a0 - lo:].float()
+        for g, (works, recvs) in enumerate(pending):
+            _wait(works)
+            for (i, t, a, b) in recvs:
+                (dk_acc if i == 0 else dv_acc)[g, a - a0:b - a0] += t.float()
+        # [ngroups, S, B, hg, D] -> [B, S, Hkv, D]
+        dk = dk_acc.to(kbuf.dtype).permute(2, 1, 0, 3, 4).reshape(B, S, ngroups * hg, D)
+        dv = dv_acc.to(vbuf.dtype).permute(2, 1, 0, 3, 4).reshape(B, S, ngroups * hg, D)
+        return dq, dk, dv, None, None, None, None, None, None, None
 
 
 class SequenceShardedElasticSparseAttention(torch.nn.Module):
@@ -188,13 +286,16 @@ class SequenceShardedElasticSparseAttention(torch.nn.Module):
     Same pattern arguments as ``ElasticSparseAttention``.  ``forward(q, k, v)``
     takes this rank's shards in sequence-major layout, q [B, S, Hq, D] and k/v
     [B, S, Hkv, D], where S = seq_len / world and rank r holds positions
-    [r*S, (r+1)*S), and returns [B, S, Hq * D].  ``ops`` is the kernel backend
-    (the CUDA library by default).
+    [r*S, (r+1)*S), and returns [B, S, Hq * D].  ``head_groups``: KV heads
+    are processed in this many groups (fewer if it does not divide
+    num_key_value_heads) so that transfers overlap kernels.  ``ops`` is the
+    kernel backend (the CUDA library by default).
     """
 
     def __init__(self, layer_idx: int, num_hidden_layers: int, num_attention_heads: int,
                  head_dim: int, attention_length: int, max_seq_len: int,
-                 num_key_value_heads: int | None = None, group=None, ops=cuda_ops):
+                 num_key_value_heads: int | None = None, group=None, ops=cuda_ops,
+                 head_groups: int = 4):
         super().__init__()
         self.spec = PatternSpec(layer_idx, num_hidden_layers, attention_length)
         self.num_attention_heads = num_attention_heads
@@ -206,6 +307,7 @@ class SequenceShardedElasticSparseAttention(torch.nn.Module):
         self.scaling = head_dim ** -0.5
         self.group = group
         self.ops = ops
+        self.head_groups = group_count(self.num_key_value_heads, head_groups)
 
     def plan(self, rows_per_rank: int, device) -> ShardPlan:
         world = dist.get_world_size(self.group)
@@ -218,10 +320,12 @@ class SequenceShardedElasticSparseAttention(torch.nn.Module):
         rank = dist.get_rank(self.group)
         if S * world > self.max_seq_len:
             raise ValueError(f"sequence length {S * world} exceeds max_seq_len {self.max_seq_len}")
+        if Hq != self.num_attention_heads or k.shape[2] != self.num_key_value_heads:
+            raise ValueError("head counts of q / k do not match the module")
         plan = self.plan(S, q.device)
         if self.ops is cuda_ops and torch.is_grad_enabled():
             from .attention import _ensure_monotone
             _ensure_monotone(Hq, self.spec, max(S * world, 2), q.device)
         out = _ShardedFunction.apply(q, k, v, self.spec, self.scaling, plan, rank, self.group,
-                                     self.ops)
+                                     self.ops, self.head_groups)
         return out.reshape(B, S, Hq * D)

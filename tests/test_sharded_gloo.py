@@ -30,27 +30,43 @@ class OracleOps:
     def _local(q, k, spec, row_offset, kv_len, kv_offset):
         Hq, n = q.shape[1], q.shape[2]
         pos = np.arange(row_offset, row_offset + n)
-        idx, mask = pattern.elastic_indices(pos, Hq, spec.attention_length, spec.layer_idx,
+        # the call's heads are heads [head_offset, head_offset + Hq) of the pattern
+        H = spec.pattern_heads or Hq
+        idx, mask = pattern.elastic_indices(pos, H, spec.attention_length, spec.layer_idx,
                                             spec.num_hidden_layers)
+        idx = idx[spec.head_offset:spec.head_offset + Hq]
+        mask = mask[spec.head_offset:spec.head_offset + Hq]
         idx = np.clip(idx, 0, kv_len - 1) - kv_offset
         assert (idx[mask.astype(bool)] >= 0).all() and (idx < k.shape[2]).all()
         return torch.from_numpy(np.clip(idx, 0, None)), torch.from_numpy(mask)
 
     @classmethod
-    def forward(cls, q, k, v, spec, scale, rows=None, row_offset=0, kv_len=None, kv_offset=0):
+    def forward(cls, q, k, v, spec, scale, rows=None, row_offset=0, kv_len=None, kv_offset=0,
+                out=None):
         idx, mask = cls._local(q, k, spec, row_offset, kv_len, kv_offset)
         do = torch.zeros_like(q)
-        out, *_ = naive.naive_forward_backward_manual(q, k, v, do, idx, mask, scale,
-                                                      q.shape[1] // k.shape[1])
-        return out.to(q.dtype), torch.zeros(q.shape[:3])
+        o, *_ = naive.naive_forward_backward_manual(q, k, v, do, idx, mask, scale,
+                                                    q.shape[1] // k.shape[1])
+        o = o.to(q.dtype)
+        if out is not None:
+            out.copy_(o)
+            o = out
+        return o, torch.zeros(q.shape[:3])
 
     @classmethod
     def backward(cls, q, k, v, o, lse, dout, spec, scale, rows=None, row_offset=0, kv_len=None,
-                 kv_offset=0):
+                 kv_offset=0, dq=None, dk=None, dv=None):
         idx, mask = cls._local(q, k, spec, row_offset, kv_len, kv_offset)
-        _, dq, dk, dv = naive.naive_forward_backward_manual(q, k, v, dout, idx, mask, scale,
+        _, gq, gk, gv = naive.naive_forward_backward_manual(q, k, v, dout, idx, mask, scale,
                                                             q.shape[1] // k.shape[1])
-        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
+        res = []
+        for got, buf, ref in ((gq, dq, q), (gk, dk, k), (gv, dv, v)):
+            got = got.to(ref.dtype)
+            if buf is not None:
+                buf.copy_(got)
+                got = buf
+            res.append(got)
+        return tuple(res)
 
 
 def _worker(rank, world, port, layer, S, Hq, Hkv, D, w, result_q, group_ranks=None):
@@ -107,6 +123,7 @@ def _free_port():
                          [(2, 7, 96, 4, 2, 16, 16, None),
                           (3, 4, 80, 2, 2, 16, 32, None),
                           (2, 0, 70, 2, 1, 8, 16, None),
+                          (2, 5, 64, 8, 4, 16, 16, None),
                           # a sequence group that is not WORLD: peers are
                           # addressed by their rank inside the group
                           (3, 6, 64, 4, 2, 16, 16, [2, 1]),
