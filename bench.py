@@ -757,12 +757,12 @@ def bench_c5(args, world, rank, local, steps=3, warmup=2):
     exchanges versus the kernels."""
     import elastic_sparse_attention_b200 as esa
     if not torch.distributed.is_initialized():
+        # one GPU: no transfers happen, a gloo group gives the module its rank
         import datetime
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         os.environ.setdefault("MASTER_PORT", "29533")
-        torch.distributed.init_process_group("nccl", rank=0, world_size=1,
-                                             timeout=datetime.timedelta(seconds=300),
-                                             device_id=torch.device("cuda", local))
+        torch.distributed.init_process_group("gloo", rank=0, world_size=1,
+                                             timeout=datetime.timedelta(seconds=300))
     dev = torch.device("cuda", local)
     S = C5_L // world
     g = torch.Generator(device=dev).manual_seed(5 + rank)

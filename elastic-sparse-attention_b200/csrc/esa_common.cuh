@@ -313,6 +313,46 @@ __device__ __forceinline__ void stg16(void* p, const uint4& v) {
   *reinterpret_cast<uint4*>(p) = v;
 }
 
+// L2 eviction-priority policies (createpolicy) for accesses that carry an
+// L2::cache_hint: evict_last for data a kernel re-reads from L2 many times
+// (the key side's q / dO rows), evict_first for data that passes once (the
+// (p, dS) workspace, the forward's probabilities), so the streams do not push
+// the re-read rows out.
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ float2 ldg_f2_hint(const float2* p, uint64_t pol) {
+  float2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.f32 {%0, %1}, [%2], %3;"
+               : "=f"(r.x), "=f"(r.y)
+               : "l"(p), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ float ldg_f32_hint(const float* p, uint64_t pol) {
+  float r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;"
+               : "=f"(r)
+               : "l"(p), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ void stg_f2_hint(float2* p, float2 v, uint64_t pol) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(p),
+               "f"(v.x), "f"(v.y), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void stg_f32_hint(float* p, float v, uint64_t pol) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v),
+               "l"(pol)
+               : "memory");
+}
+
 // Butterfly "transpose-reduce": every lane of an aligned group of LPR lanes
 // holds LPR partial sums v[0..LPR); afterwards lane r of the group holds in
 // v[0] the total of index r over the group.  Costs LPR-1 shuffles per lane.

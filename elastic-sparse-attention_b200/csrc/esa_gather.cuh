@@ -236,15 +236,35 @@ __device__ __forceinline__ void tile_slot_rows(const AttnParams& p, int j, int h
 // ---------------------------------------------------------------------------
 constexpr int kTilePairs = 128;
 constexpr int kTileMaxW = 64;
-// Row strides of the per-pair shared arrays are odd in 32-bit words (65, and
-// 66 halves = 33 words) so that the pairs a warp touches fall in different banks.
+// Per-pair shared arrays.  The row indices (int) and the 16-bit weights are
+// read 2 slots at a time (8-byte / 4-byte loads), so their rows are 68
+// elements long: 16- resp. 8-byte aligned, and the two pairs one warp load
+// reads (neighbouring pairs) start 4 (2) banks apart, clear of each other.
+// The fp32 score rows keep an odd stride of 65 words (read one slot at a
+// time by one thread per pair).
+constexpr int kTileRowStride = kTileMaxW + 4;
 constexpr int kTileIdxStride = kTileMaxW + 1;
-constexpr int kTileSpStride = kTileMaxW + 2;
-constexpr int kTileSidxBytes = kTilePairs * kTileIdxStride * 4;
+constexpr int kTileSpStride = kTileMaxW + 4;
+constexpr int kTileSidxBytes = kTilePairs * kTileRowStride * 4;
+constexpr int kTileScoreBytes = kTilePairs * kTileIdxStride * 4;
 // sidx, fp32 scores (later the weights in the input type), per-pair 1 / sum.
 // Kept small: shared memory comes out of the same 256 KB per SM as the L1
 // that serves the shared K / V rows.
-constexpr int kTileSmemBytes = 2 * kTileSidxBytes + kTilePairs * 4;
+constexpr int kTileSmemBytes = kTileSidxBytes + kTileScoreBytes + kTilePairs * 4;
+static_assert(kTilePairs * kTileSpStride * 2 <= kTileScoreBytes, "weights alias the scores");
+
+// Rows of 2 consecutive slots of one pair (one 8-byte shared load).
+__device__ __forceinline__ int2 slot_rows2(const int (*sidx)[kTileRowStride], int pi, int k0) {
+  return *reinterpret_cast<const int2*>(&sidx[pi][k0]);
+}
+__device__ __forceinline__ int row2_at(const int2& r, int i) { return i ? r.y : r.x; }
+// 2 consecutive 16-bit weights of one pair (one 4-byte shared load).
+__device__ __forceinline__ uint32_t weights2(const uint16_t* row, int k0) {
+  return *reinterpret_cast<const uint32_t*>(row + k0);
+}
+__device__ __forceinline__ uint16_t weight2_at(uint32_t u, int i) {
+  return static_cast<uint16_t>(i ? (u >> 16) : (u & 0xffffu));
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(256, 2)
@@ -259,13 +279,13 @@ fwd_tile_kernel(const AttnParams p) {
   static_assert(MI * 2 == LPR, "two slots per transpose-reduce");
   constexpr int HALF = kTileMaxW / 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  int(*sidx)[kTileIdxStride] = reinterpret_cast<int(*)[kTileIdxStride]>(smem_raw);
+  int(*sidx)[kTileRowStride] = reinterpret_cast<int(*)[kTileRowStride]>(smem_raw);
   // fp32 scores; after the softmax the same bytes hold the weights in the
   // input type, laid out as Sc[kTilePairs][kTileSpStride]
   float(*sbuf)[kTileIdxStride] =
       reinterpret_cast<float(*)[kTileIdxStride]>(smem_raw + kTileSidxBytes);
   Sc(*sp)[kTileSpStride] = reinterpret_cast<Sc(*)[kTileSpStride]>(&sbuf[0][0]);
-  float* sl = reinterpret_cast<float*>(smem_raw + 2 * kTileSidxBytes);
+  float* sl = reinterpret_cast<float*>(smem_raw + kTileSidxBytes + kTileScoreBytes);
   const int w = p.pat.w;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane / LPR, r = lane % LPR;
@@ -300,25 +320,27 @@ fwd_tile_kernel(const AttnParams p) {
                                           h * p.sqh + (int64_t)j * p.sqs + r * EPL)
                            : make_uint4(0, 0, 0, 0);
     }
-    // ---- scores, two slots per butterfly: lane r ends with slot k0 + r / MI
-    // of pair pw0 + (r % MI) * RPW + g --------------------------------------
+    // ---- scores, two slots per butterfly (their rows in one shared load per
+    // pair): lane r ends with slot k0 + r / MI of pair pw0 + (r % MI) * RPW + g.
+    // A slot past w (odd w) holds a masked row (tile_slot_rows) ----------------
     const int my_pi = pw0 + (r % MI) * RPW + g;
     for (int k0 = 0; k0 < w; k0 += 2) {
+      int2 rows[MI];
+#pragma unroll
+      for (int m = 0; m < MI; ++m) rows[m] = slot_rows2(sidx, pw0 + m * RPW + g, k0);
       float part[LPR];
 #pragma unroll
       for (int s2 = 0; s2 < 2; ++s2) {
         uint4 kb[MI];
 #pragma unroll
-        for (int m = 0; m < MI; ++m) {
-          const int row = sidx[pw0 + m * RPW + g][k0 + s2];
-          kb[m] = ldg16(Kb + (int64_t)(row & kRowMask) * p.sks);
-        }
+        for (int m = 0; m < MI; ++m)
+          kb[m] = ldg16(Kb + (int64_t)(row2_at(rows[m], s2) & kRowMask) * p.sks);
 #pragma unroll
         for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(qv[m], kb[m], 0.f);
       }
       transpose_reduce<LPR>(part, lane);
       const int k = k0 + r / MI;
-      if (k < kTileMaxW) sbuf[my_pi][k] = sidx[my_pi][k] >= 0 ? part[0] * p.scale_log2 : -INFINITY;
+      sbuf[my_pi][k] = sidx[my_pi][k] >= 0 ? part[0] * p.scale_log2 : -INFINITY;
     }
   }
   __syncthreads();
@@ -357,10 +379,11 @@ fwd_tile_kernel(const AttnParams p) {
     // [B, Hq, w, n]; the 4 bytes of neighbouring queries come from
     // neighbouring warps and merge in L2
     if (p.probs && j < p.n_rows) {
+      const uint64_t pol = l2_evict_first_policy();   // read once, by the backward
       float* dst = p.probs + ((int64_t)(b * p.Hq + h) * w + kbeg) * p.n_rows + j;
 #pragma unroll
       for (int i = 0; i < HALF; ++i)
-        if (kbeg + i < w) dst[(int64_t)i * p.n_rows] = exp2f(v[i] - mx) * inv;
+        if (kbeg + i < w) stg_f32_hint(dst + (int64_t)i * p.n_rows, exp2f(v[i] - mx) * inv, pol);
     }
   }
   __syncthreads();
@@ -371,15 +394,25 @@ fwd_tile_kernel(const AttnParams p) {
   for (int m = 0; m < MI; ++m)
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[m][e] = 0.f;
-  for (int k = 0; k < w; ++k) {
-    uint4 vb[MI];
+  // 2 slots per shared load of rows and weights; a slot past w (odd w) has
+  // weight 0 (written by the softmax) and a masked in-bounds row
+  for (int k0 = 0; k0 < w; k0 += 2) {
+    int2 rows[MI];
+    uint32_t wts[MI];
 #pragma unroll
     for (int m = 0; m < MI; ++m) {
-      const int row = sidx[pw0 + m * RPW + g][k];
-      vb[m] = ldg16(Vb + (int64_t)(row & kRowMask) * p.svs);
+      rows[m] = slot_rows2(sidx, pw0 + m * RPW + g, k0);
+      wts[m] = weights2(&sp[pw0 + m * RPW + g][0], k0);
     }
 #pragma unroll
-    for (int m = 0; m < MI; ++m) M::axpy(sp[pw0 + m * RPW + g][k], vb[m], acc[m]);
+    for (int i = 0; i < 2; ++i) {
+      uint4 vb[MI];
+#pragma unroll
+      for (int m = 0; m < MI; ++m)
+        vb[m] = ldg16(Vb + (int64_t)(row2_at(rows[m], i) & kRowMask) * p.svs);
+#pragma unroll
+      for (int m = 0; m < MI; ++m) M::axpy(weight2_at(wts[m], i), vb[m], acc[m]);
+    }
   }
 #pragma unroll
   for (int m = 0; m < MI; ++m) {
@@ -404,7 +437,8 @@ fwd_tile_kernel(const AttnParams p) {
 // Every pass walks the slots with all warps together, so the K / V rows the
 // tile's pairs share come from L1.
 // ---------------------------------------------------------------------------
-constexpr int kTileBwdSmemBytes = 2 * kTileSidxBytes + kTilePairs * kTileSpStride * 2;   // 16-bit dS
+constexpr int kTileBwdSmemBytes = kTileSidxBytes + kTileScoreBytes +
+                                  kTilePairs * kTileSpStride * 2;   // 16-bit dS
 
 template <typename T, int D>
 __global__ void __launch_bounds__(256, 2)
@@ -419,10 +453,11 @@ bwd_query_tile_kernel(const AttnParams p) {
   static_assert(MI * 2 == LPR, "two slots per transpose-reduce");
   constexpr int HALF = kTileMaxW / 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  int(*sidx)[kTileIdxStride] = reinterpret_cast<int(*)[kTileIdxStride]>(smem_raw);
+  int(*sidx)[kTileRowStride] = reinterpret_cast<int(*)[kTileRowStride]>(smem_raw);
   float(*sprob)[kTileIdxStride] =
       reinterpret_cast<float(*)[kTileIdxStride]>(smem_raw + kTileSidxBytes);
-  Sc(*sds)[kTileSpStride] = reinterpret_cast<Sc(*)[kTileSpStride]>(smem_raw + 2 * kTileSidxBytes);
+  Sc(*sds)[kTileSpStride] =
+      reinterpret_cast<Sc(*)[kTileSpStride]>(smem_raw + kTileSidxBytes + kTileScoreBytes);
   const int w = p.pat.w;
   const int n = p.n_rows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -460,12 +495,13 @@ bwd_query_tile_kernel(const AttnParams p) {
   // ---- pass 1a: p = exp2(s * scale_log2 - lse), or the forward's p --------
   if (p.probs) {
     const int lg = __ffs(G) - 1;   // same lane order as the forward's write
+    const uint64_t pol = l2_evict_first_policy();
     for (int k = warp; k < w; k += 8) {
       for (int pi = lane; pi < kTilePairs; pi += 32) {
         const int j = j0 + (pi >> lg);
         if (j >= n) break;
         const int h = hkv * G + (pi & (G - 1));
-        sprob[pi][k] = p.probs[(((int64_t)b * p.Hq + h) * w + k) * n + j];
+        sprob[pi][k] = ldg_f32_hint(p.probs + (((int64_t)b * p.Hq + h) * w + k) * n + j, pol);
       }
     }
     __syncthreads();
@@ -475,15 +511,16 @@ bwd_query_tile_kernel(const AttnParams p) {
 #pragma unroll
     for (int m = 0; m < MI; ++m) qv[m] = row_of(p.q, p.sqb, p.sqh, p.sqs, m);
     for (int k0 = 0; k0 < w; k0 += 2) {
+      int2 rows[MI];
+#pragma unroll
+      for (int m = 0; m < MI; ++m) rows[m] = slot_rows2(sidx, pw0 + m * RPW + g, k0);
       float part[LPR];
 #pragma unroll
       for (int s2 = 0; s2 < 2; ++s2) {
         uint4 kb[MI];
 #pragma unroll
-        for (int m = 0; m < MI; ++m) {
-          const int row = sidx[pw0 + m * RPW + g][k0 + s2];
-          kb[m] = ldg16(Kb + (int64_t)(row & kRowMask) * p.sks);
-        }
+        for (int m = 0; m < MI; ++m)
+          kb[m] = ldg16(Kb + (int64_t)(row2_at(rows[m], s2) & kRowMask) * p.sks);
 #pragma unroll
         for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(qv[m], kb[m], 0.f);
       }
@@ -507,24 +544,27 @@ bwd_query_tile_kernel(const AttnParams p) {
 #pragma unroll
     for (int m = 0; m < MI; ++m) my_delta = (r % MI) == m ? delta[m] : my_delta;
     float2* pds_pair = p.pds + ((int64_t)(b * p.Hq + my_h) * w) * n + my_j;
+    const uint64_t pol_ws = l2_evict_first_policy();   // read once, by the key side
     for (int k0 = 0; k0 < w; k0 += 2) {
+      int2 rows[MI];
+#pragma unroll
+      for (int m = 0; m < MI; ++m) rows[m] = slot_rows2(sidx, pw0 + m * RPW + g, k0);
       float part[LPR];
 #pragma unroll
       for (int s2 = 0; s2 < 2; ++s2) {
         uint4 vb[MI];
 #pragma unroll
-        for (int m = 0; m < MI; ++m) {
-          const int row = sidx[pw0 + m * RPW + g][k0 + s2];
-          vb[m] = ldg16(Vb + (int64_t)(row & kRowMask) * p.svs);
-        }
+        for (int m = 0; m < MI; ++m)
+          vb[m] = ldg16(Vb + (int64_t)(row2_at(rows[m], s2) & kRowMask) * p.svs);
 #pragma unroll
         for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(dv[m], vb[m], 0.f);
       }
       transpose_reduce<LPR>(part, lane);
       const int k = k0 + r / MI;
-      const float pk = sprob[my_pi][k];
+      // a slot past w (odd w) gets p = dS = 0: pass 2 reads it
+      const float pk = k < w ? sprob[my_pi][k] : 0.f;
       const float dsk = pk * (part[0] - my_delta) * p.scale;   // 0 for masked slots
-      if (my_live && k < w) pds_pair[(int64_t)k * n] = make_float2(pk, dsk);
+      if (my_live && k < w) stg_f2_hint(pds_pair + (int64_t)k * n, make_float2(pk, dsk), pol_ws);
       sds[my_pi][k] = M::scalar(dsk);
     }
   }
@@ -536,15 +576,23 @@ bwd_query_tile_kernel(const AttnParams p) {
   for (int m = 0; m < MI; ++m)
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[m][e] = 0.f;
-  for (int k = 0; k < w; ++k) {
-    uint4 kb[MI];
+  for (int k0 = 0; k0 < w; k0 += 2) {
+    int2 rows[MI];
+    uint32_t wts[MI];
 #pragma unroll
     for (int m = 0; m < MI; ++m) {
-      const int row = sidx[pw0 + m * RPW + g][k];
-      kb[m] = ldg16(Kb + (int64_t)(row & kRowMask) * p.sks);
+      rows[m] = slot_rows2(sidx, pw0 + m * RPW + g, k0);
+      wts[m] = weights2(&sds[pw0 + m * RPW + g][0], k0);
     }
 #pragma unroll
-    for (int m = 0; m < MI; ++m) M::axpy(sds[pw0 + m * RPW + g][k], kb[m], acc[m]);
+    for (int i = 0; i < 2; ++i) {
+      uint4 kb[MI];
+#pragma unroll
+      for (int m = 0; m < MI; ++m)
+        kb[m] = ldg16(Kb + (int64_t)(row2_at(rows[m], i) & kRowMask) * p.sks);
+#pragma unroll
+      for (int m = 0; m < MI; ++m) M::axpy(weight2_at(wts[m], i), kb[m], acc[m]);
+    }
   }
 #pragma unroll
   for (int m = 0; m < MI; ++m) {

@@ -112,9 +112,12 @@ __device__ __forceinline__ T round_to(float x) {
 __device__ __forceinline__ void km_cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
-__device__ __forceinline__ void km_cp_async16s(uint32_t smem_dst, const void* gmem_src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_dst), "l"(gmem_src),
-               "r"(valid ? 16 : 0)
+// 16-byte copy global -> shared (L1 bypassed), zero-filled when !valid, with
+// an L2 eviction policy for the source line.
+__device__ __forceinline__ void km_cp_async16s(uint32_t smem_dst, const void* gmem_src, bool valid,
+                                               uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(smem_dst),
+               "l"(gmem_src), "r"(valid ? 16 : 0), "l"(pol)
                : "memory");
 }
 template <int N>
@@ -146,6 +149,10 @@ bwd_key_mma_kernel(const AttnParams p) {
   if (lr0 >= p.kv_rows) return;
   const int n = p.n_rows;
   const int kvmax = p.kv_len - 1;
+  // L2: the users' q / dO rows are re-read (a query row serves 64 keys spread
+  // over the sweep); the (p, dS) workspace passes once
+  const uint64_t pol_rows = l2_evict_last_policy();
+  const uint64_t pol_stream = l2_evict_first_policy();
   // col -> (hh, k) with hh = col / w by a multiply-high (exact for col < 2^14, w <= 1024)
   const unsigned long long wmagic = 0xffffffffull / (unsigned)w + 1ull;
   // lane j (< GS) holds the head weight of query head hkv * G + hh0 + j
@@ -284,7 +291,7 @@ bwd_key_mma_kernel(const AttnParams p) {
         c_f = resolve(t0, qi_f);
         // past the end: slot 0 of column base 0 (in bounds), weights zeroed
         if (!valid) { qi_f = 0; c_f.hh = 0; c_f.base = 0; }
-        const float2 pd = p.pds[(int64_t)c_f.base * n + qi_f];
+        const float2 pd = ldg_f2_hint(p.pds + (int64_t)c_f.base * n + qi_f, pol_stream);
         r.pd = valid ? pd : make_float2(0.f, 0.f);
         r.oq = (uint32_t)c_f.hh * qh16 + (uint32_t)qi_f * qs16;
         r.od = (uint32_t)c_f.hh * dh16 + (uint32_t)qi_f * ds16;
@@ -304,8 +311,8 @@ bwd_key_mma_kernel(const AttnParams p) {
           const bool ok = t0 + 16 * h + x < total;
           const uint32_t dst = stage + m * C::kUsersPerCopy * C::kUserBytes +
                                (((uint32_t)cp_chunk ^ (uint32_t)(x & 7)) << 4);
-          km_cp_async16s(dst, qlane + (size_t)oq * 16u, ok);
-          km_cp_async16s(dst + C::kRowBytes, dlane + (size_t)od * 16u, ok);
+          km_cp_async16s(dst, qlane + (size_t)oq * 16u, ok, pol_rows);
+          km_cp_async16s(dst + C::kRowBytes, dlane + (size_t)od * 16u, ok, pol_rows);
         }
         km_cp_async_commit();
       };

@@ -6,7 +6,8 @@
 // (query, head) pairs of one KV head (128 / G queries x G heads), warp w owns
 // pairs [16w, 16w + 16), half a warp load is one 256-byte row; all warps walk
 // the slots together, K rows first (the score pass), then V rows (the P V
-// pass), two slots per step.  The rows come from the elastic pattern (the
+// pass), two slots per step with their rows in one shared load.  The
+// rows come from the elastic pattern (the
 // tile kernels' exact stream), uniformly at random over the KV head's rows
 // (an L2-resident random gather), or at random within 64 rows per CTA (an
 // L1-resident gather).  The loaded words are folded into an xor checksum
@@ -38,7 +39,7 @@ gather_probe_kernel(const AttnParams p, uint32_t* sink) {
   constexpr int MI = PPW / RPW;            // warp loads per slot
   constexpr int HALF = kTileMaxW / 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  int(*sidx)[kTileIdxStride] = reinterpret_cast<int(*)[kTileIdxStride]>(smem_raw);
+  int(*sidx)[kTileRowStride] = reinterpret_cast<int(*)[kTileRowStride]>(smem_raw);
   const int w = p.pat.w;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane / LPR, r = lane % LPR;
@@ -57,11 +58,17 @@ gather_probe_kernel(const AttnParams p, uint32_t* sink) {
   const int win0 = MODE == kProbeL1Window
                        ? (int)(probe_mix(cta) % (uint32_t)(p.kv_rows - kProbeWindowRows + 1))
                        : 0;
-  auto row_at = [&](int pi, int k) -> int {
-    if (MODE == kProbePattern) return sidx[pi][k] & kRowMask;
-    const uint32_t hsh = probe_mix(cta * 8192u + (uint32_t)(pi * kTileMaxW + k));
-    if (MODE == kProbeL2Random) return (int)(hsh % (uint32_t)p.kv_rows);
-    return win0 + (int)(hsh & (kProbeWindowRows - 1));
+  // rows of 2 slots of pair pi (a slot past w: the masked in-bounds row)
+  auto rows_at = [&](int pi, int k0) -> int2 {
+    if (MODE == kProbePattern) return slot_rows2(sidx, pi, k0);
+    int v[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t hsh = probe_mix(cta * 8192u + (uint32_t)(pi * kTileMaxW + k0 + i));
+      v[i] = MODE == kProbeL2Random ? (int)(hsh % (uint32_t)p.kv_rows)
+                                    : win0 + (int)(hsh & (kProbeWindowRows - 1));
+    }
+    return make_int2(v[0], v[1]);
   };
   const int pw0 = warp * PPW;
   const T* Kb = reinterpret_cast<const T*>(p.k) + b * p.skb + hkv * p.skh + r * EPL;
@@ -72,14 +79,15 @@ gather_probe_kernel(const AttnParams p, uint32_t* sink) {
     const T* base = pass ? Vb : Kb;
     const int64_t stride = pass ? p.svs : p.sks;
     for (int k0 = 0; k0 < w; k0 += 2) {
+      int2 rows[MI];
+#pragma unroll
+      for (int m = 0; m < MI; ++m) rows[m] = rows_at(pw0 + m * RPW + g, k0);
       uint4 x[2][MI];
 #pragma unroll
       for (int s2 = 0; s2 < 2; ++s2)
 #pragma unroll
-        for (int m = 0; m < MI; ++m) {
-          const int k = min(k0 + s2, w - 1);
-          x[s2][m] = ldg16(base + (int64_t)row_at(pw0 + m * RPW + g, k) * stride);
-        }
+        for (int m = 0; m < MI; ++m)
+          x[s2][m] = ldg16(base + (int64_t)(row2_at(rows[m], s2) & kRowMask) * stride);
 #pragma unroll
       for (int s2 = 0; s2 < 2; ++s2)
 #pragma unroll

@@ -97,15 +97,20 @@ def make_plan(num_heads: int, spec: PatternSpec, rows_per_rank: int, world: int,
 
 # ---------------------------------------------------------------------------
 # Optional per-step timing of one rank (profile_step): CUDA events on the
-# compute stream around the kernels and around each wait for a transfer.
+# compute stream around the kernels and around each wait for a transfer.  The
+# record list is process-wide: the backward runs on autograd's own thread.
 # ---------------------------------------------------------------------------
-_timing = threading.local()
+class _Timing:
+    records = None
+
+
+_timing = _Timing()
 
 
 class _Span:
     def __init__(self, kind: str):
         self.kind = kind
-        self.rec = getattr(_timing, "records", None)
+        self.rec = _timing.records
 
     def __enter__(self):
         if self.rec is not None:
