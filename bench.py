@@ -211,8 +211,9 @@ def family_bytes(nh, nkv, key_heads_per_launch=2):
     """Per layer and kernel family: (algorithmic bytes = what the family's
     role must read and write, implementation bytes = this build's own
     intermediates).  The tile forward leaves fp32 probabilities for the
-    backward; the query side reads them and writes (p, dS) per (row, slot);
-    the key side reads (p, dS) and, with GQA, sums its launches in fp32."""
+    backward; the query side reads them and writes (p, dS) per (row, slot)
+    (its row value sum(p dP) needs no O read); the key side reads (p, dS)
+    and, with GQA, sums its launches in fp32."""
     q_b, kv_b, lse_b = B * nh * L * D * ES, B * nkv * L * D * ES, B * nh * L * 4
     probs_b, pds_b = B * nh * W * L * 4, B * nh * W * L * 8
     g = nh // nkv
@@ -221,7 +222,7 @@ def family_bytes(nh, nkv, key_heads_per_launch=2):
     fwd, bwd = layer_bytes(nh, nkv)
     return {"fwd_window": (fwd, 0), "fwd_tile": (fwd, probs_b),
             "bwd_window": (bwd, 2 * lse_b),
-            "bwd_query": (3 * q_b + 2 * kv_b, probs_b + pds_b),
+            "bwd_query": (2 * q_b + 2 * kv_b, probs_b + pds_b),   # dO, K, V in; dQ out
             "bwd_key": (2 * q_b + 2 * kv_b, pds_b + acc_b),
             "bwd_heavy": (0, 0)}
 

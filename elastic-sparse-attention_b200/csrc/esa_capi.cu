@@ -214,6 +214,16 @@ constexpr int kKeyRowsPerWarp = 16;
 
 int rows_per_cta(int G) { return G >= 64 ? 1 : 64 / G; }
 
+// Number of SMs of the current device (persistent kernels launch one CTA per SM).
+int sm_count(int* out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(out, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess || *out < 1)
+    return fail(ESA_ERR_CUDA, "cannot read the SM count: %s", cudaGetErrorString(e));
+  return ESA_OK;
+}
+
 // Per-device addresses of a __device__ variable of this library, looked up
 // once per device (cudaGetSymbolAddress with that device current) and cached.
 constexpr int kMaxDevices = 64;
@@ -391,9 +401,14 @@ int launch_window(const esa::AttnParams& p, cudaStream_t s) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            esa::kWinSmemBytes) != cudaSuccess)
     return fail(ESA_ERR_CUDA, "cannot reserve shared memory for the window path");
-  dim3 grid((p.n_rows + QT - 1) / QT, p.Hkv * (p.G / HT), p.B);
+  // persistent: one CTA per SM walks the (query tile, head group, batch) tiles
+  const int64_t tiles = (int64_t)((p.n_rows + QT - 1) / QT) * (p.Hkv * (p.G / HT)) * p.B;
+  if (tiles > INT32_MAX) return fail(ESA_ERR_UNSUPPORTED, "window path: too many tiles");
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  const int grid = (int)std::min<int64_t>(tiles, sms);
   LaunchTrace tr("window_fwd_tc", s);
-  kern<<<grid, esa::kWinThreads, esa::kWinSmemBytes, s>>>(maps, p, nk);
+  kern<<<grid, esa::kWinThreads, esa::kWinSmemBytes, s>>>(maps, p, nk, (int)tiles);
   return check_launch("forward (tensor-core window)");
 }
 
@@ -424,10 +439,15 @@ int launch_window_bwd(const esa::AttnParams& p, cudaStream_t s) {
       cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            esa::kWbkSmemBytes) != cudaSuccess)
     return fail(ESA_ERR_CUDA, "cannot reserve shared memory for the window backward");
-  dim3 gq((p.n_rows + QT - 1) / QT, p.Hkv * (p.G / HT), p.B);
+  // dQ: persistent, one CTA per SM over the (query tile, head group, batch) tiles
+  const int64_t tiles = (int64_t)((p.n_rows + QT - 1) / QT) * (p.Hkv * (p.G / HT)) * p.B;
+  if (tiles > INT32_MAX) return fail(ESA_ERR_UNSUPPORTED, "window backward: too many tiles");
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  const int gq = (int)std::min<int64_t>(tiles, sms);
   {
     LaunchTrace tr("window_bwd_dq_tc", s);
-    kq<<<gq, esa::kWinBwdThreads, esa::kWbqSmemBytes, s>>>(a, p, nk, delta);
+    kq<<<gq, esa::kWbqThreads, esa::kWbqSmemBytes, s>>>(a, p, nk, (int)tiles, delta);
   }
   if (int rc = check_launch("backward (tensor-core window, dQ)")) return rc;
   dim3 gk((p.kv_rows + esa::kWbkKeys - 1) / esa::kWbkKeys, p.Hkv, p.B);
@@ -491,9 +511,11 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
   if constexpr (!std::is_same<T, float>::value && D == esa::kWinHeadDim) {
     if (p.n_rows > 0 && !(p.flags & ESA_FLAG_GATHER_ONLY) && p.sdob > 0 && p.sdoh > 0 &&
         p.sdos > 0) {
+      // the tensor-core backward takes up to kWbqMaxKeys keys per tile
       const int ht = window_heads<T, D>(p, p.alpha_zero, p.flags);
-      if (ht == 4) return launch_window_bwd<T, 4>(p, s);
-      if (ht == 2) return launch_window_bwd<T, 2>(p, s);
+      const int nk = ht ? (esa::kWinRows / ht + p.pat.w - 1 + 15) / 16 * 16 : 0;
+      if (ht == 4 && nk <= esa::kWbqMaxKeys) return launch_window_bwd<T, 4>(p, s);
+      if (ht == 2 && nk <= esa::kWbqMaxKeys) return launch_window_bwd<T, 2>(p, s);
     }
   }
   bool query_done = false;

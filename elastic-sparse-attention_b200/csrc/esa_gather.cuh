@@ -253,6 +253,21 @@ constexpr int kTileScoreBytes = kTilePairs * kTileIdxStride * 4;
 constexpr int kTileSmemBytes = kTileSidxBytes + kTileScoreBytes + kTilePairs * 4;
 static_assert(kTilePairs * kTileSpStride * 2 <= kTileScoreBytes, "weights alias the scores");
 
+// Lane layout of the tile kernels: a 16-bit row of D elements is read by
+// LPR = 8 lanes, each taking CPL 16-byte chunks (chunks r and r + 8 of the
+// row for lane r of its group): a warp load instruction then covers RPW = 4
+// whole 128-byte segments of 4 rows (4 L1 wavefronts for 512 bytes, as with
+// one chunk per lane), while a dot product is finished by a butterfly over 8
+// lanes (7 shuffles for two slots of the warp's 16 pairs) instead of 16.
+template <typename T, int D>
+struct TileLayout {
+  static constexpr int EPL = Vec<T>::kElems;   // elements per 16-byte chunk
+  static constexpr int LPR = 8;                // lanes per row
+  static constexpr int CPL = D / (EPL * LPR);  // chunks per lane
+  static constexpr int RPW = 32 / LPR;         // rows per warp load
+  static_assert(CPL >= 1 && CPL * EPL * LPR == D, "tile kernels take D = 64 or 128 (16-bit)");
+};
+
 // Rows of 2 consecutive slots of one pair (one 8-byte shared load).
 __device__ __forceinline__ int2 slot_rows2(const int (*sidx)[kTileRowStride], int pi, int k0) {
   return *reinterpret_cast<const int2*>(&sidx[pi][k0]);
@@ -269,11 +284,11 @@ __device__ __forceinline__ uint16_t weight2_at(uint32_t u, int i) {
 template <typename T, int D>
 __global__ void __launch_bounds__(256, 2)
 fwd_tile_kernel(const AttnParams p) {
-  using L = Layout<T, D>;
+  using L = TileLayout<T, D>;
   using V = Vec<T>;
   using M = Mix<T>;
   using Sc = typename M::Scalar;
-  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW, CPL = L::CPL;
   constexpr int PPW = kTilePairs / 8;      // pairs per warp
   constexpr int MI = PPW / RPW;            // warp loads per slot
   static_assert(MI * 2 == LPR, "two slots per transpose-reduce");
@@ -305,20 +320,23 @@ fwd_tile_kernel(const AttnParams p) {
   __syncthreads();
 
   const int pw0 = warp * PPW;   // first pair of this warp
+  // lane r of a group reads chunks r, r + LPR, ... of a row
   const T* Kb = reinterpret_cast<const T*>(p.k) + b * p.skb + hkv * p.skh + r * EPL;
   const T* Vb = reinterpret_cast<const T*>(p.v) + b * p.svb + hkv * p.svh + r * EPL;
 
   {
     // q chunks of this lane's pairs (pair pw0 + m * RPW + g, m < MI)
-    uint4 qv[MI];
+    uint4 qv[MI][CPL];
 #pragma unroll
     for (int m = 0; m < MI; ++m) {
       const int pi = pw0 + m * RPW + g;
       const int j = j0 + pi / G;
       const int h = hkv * G + pi % G;
-      qv[m] = j < p.n_rows ? ldg16_stream(reinterpret_cast<const T*>(p.q) + b * p.sqb +
-                                          h * p.sqh + (int64_t)j * p.sqs + r * EPL)
-                           : make_uint4(0, 0, 0, 0);
+      const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh + (int64_t)j * p.sqs +
+                      r * EPL;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c)
+        qv[m][c] = j < p.n_rows ? ldg16_stream(qrow + c * LPR * EPL) : make_uint4(0, 0, 0, 0);
     }
     // ---- scores, two slots per butterfly (their rows in one shared load per
     // pair): lane r ends with slot k0 + r / MI of pair pw0 + (r % MI) * RPW + g.
@@ -331,12 +349,20 @@ fwd_tile_kernel(const AttnParams p) {
       float part[LPR];
 #pragma unroll
       for (int s2 = 0; s2 < 2; ++s2) {
-        uint4 kb[MI];
+        uint4 kb[MI][CPL];
 #pragma unroll
-        for (int m = 0; m < MI; ++m)
-          kb[m] = ldg16(Kb + (int64_t)(row2_at(rows[m], s2) & kRowMask) * p.sks);
+        for (int m = 0; m < MI; ++m) {
+          const T* krow = Kb + (int64_t)(row2_at(rows[m], s2) & kRowMask) * p.sks;
 #pragma unroll
-        for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(qv[m], kb[m], 0.f);
+          for (int c = 0; c < CPL; ++c) kb[m][c] = ldg16(krow + c * LPR * EPL);
+        }
+#pragma unroll
+        for (int m = 0; m < MI; ++m) {
+          float d = 0.f;
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) d = M::dot(qv[m][c], kb[m][c], d);
+          part[s2 * MI + m] = d;
+        }
       }
       transpose_reduce<LPR>(part, lane);
       const int k = k0 + r / MI;
@@ -388,12 +414,12 @@ fwd_tile_kernel(const AttnParams p) {
   }
   __syncthreads();
 
-  // ---- O = P V: lane keeps the EPL output dims r*EPL.. of its MI pairs ----
-  float acc[MI][EPL];
+  // ---- O = P V: lane keeps dims (r + c * LPR) * EPL .. of its MI pairs ----
+  float acc[MI][CPL * EPL];
 #pragma unroll
   for (int m = 0; m < MI; ++m)
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) acc[m][e] = 0.f;
+    for (int e = 0; e < CPL * EPL; ++e) acc[m][e] = 0.f;
   // 2 slots per shared load of rows and weights; a slot past w (odd w) has
   // weight 0 (written by the softmax) and a masked in-bounds row
   for (int k0 = 0; k0 < w; k0 += 2) {
@@ -406,12 +432,17 @@ fwd_tile_kernel(const AttnParams p) {
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      uint4 vb[MI];
+      uint4 vb[MI][CPL];
+#pragma unroll
+      for (int m = 0; m < MI; ++m) {
+        const T* vrow = Vb + (int64_t)(row2_at(rows[m], i) & kRowMask) * p.svs;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) vb[m][c] = ldg16(vrow + c * LPR * EPL);
+      }
 #pragma unroll
       for (int m = 0; m < MI; ++m)
-        vb[m] = ldg16(Vb + (int64_t)(row2_at(rows[m], i) & kRowMask) * p.svs);
 #pragma unroll
-      for (int m = 0; m < MI; ++m) M::axpy(weight2_at(wts[m], i), vb[m], acc[m]);
+        for (int c = 0; c < CPL; ++c) M::axpy(weight2_at(wts[m], i), vb[m][c], acc[m] + c * EPL);
     }
   }
 #pragma unroll
@@ -422,32 +453,36 @@ fwd_tile_kernel(const AttnParams p) {
     if (j < p.n_rows) {
       const float inv = sl[pi];
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) acc[m][e] *= inv;
+      for (int e = 0; e < CPL * EPL; ++e) acc[m][e] *= inv;
       T* orow = reinterpret_cast<T*>(p.o) + b * p.sob + h * p.soh + (int64_t)j * p.sos + r * EPL;
-      stg16(orow, V::from_float(acc[m]));
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) stg16(orow + c * LPR * EPL, V::from_float(acc[m] + c * EPL));
     }
   }
 }
 
 // ---------------------------------------------------------------------------
 // Backward, query side, slot-major tile variant (same tiling as
-// fwd_tile_kernel): pass 1a scores -> p = exp2(s - lse) (fp32, shared), pass
-// 1b dp = dO.v -> dS = p (dp - rowsum(dO O)), written to the (p, dS*scale)
-// workspace and kept in the input type in shared memory, pass 2 dQ = sum dS k.
+// fwd_tile_kernel): pass 1a scores -> p = exp2(s - lse) (fp32, shared), or the
+// forward's probabilities; pass 1b dp = dO.v (V gather, fp32, shared) and the
+// row value delta = sum_k p_k dp_k, which equals rowsum(dO o O) for the exact
+// O = sum_k p_k v_k (computed this way it needs no O read and carries no
+// rounding of the stored 16-bit O: a key with ~1e5 users sums that rounding
+// into its dK otherwise); then dS = p (dp - delta), written to the (p,
+// dS*scale) workspace and kept in shared memory; pass 2 dQ = sum dS k.
 // Every pass walks the slots with all warps together, so the K / V rows the
 // tile's pairs share come from L1.
 // ---------------------------------------------------------------------------
-constexpr int kTileBwdSmemBytes = kTileSidxBytes + kTileScoreBytes +
-                                  kTilePairs * kTileSpStride * 2;   // 16-bit dS
+constexpr int kTileBwdSmemBytes = kTileSidxBytes + 2 * kTileScoreBytes;   // sidx, p, dp / dS
 
 template <typename T, int D>
 __global__ void __launch_bounds__(256, 2)
 bwd_query_tile_kernel(const AttnParams p) {
-  using L = Layout<T, D>;
+  using L = TileLayout<T, D>;
   using V = Vec<T>;
   using M = Mix<T>;
   using Sc = typename M::Scalar;
-  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW, CPL = L::CPL;
   constexpr int PPW = kTilePairs / 8;
   constexpr int MI = PPW / RPW;
   static_assert(MI * 2 == LPR, "two slots per transpose-reduce");
@@ -456,8 +491,9 @@ bwd_query_tile_kernel(const AttnParams p) {
   int(*sidx)[kTileRowStride] = reinterpret_cast<int(*)[kTileRowStride]>(smem_raw);
   float(*sprob)[kTileIdxStride] =
       reinterpret_cast<float(*)[kTileIdxStride]>(smem_raw + kTileSidxBytes);
-  Sc(*sds)[kTileSpStride] =
-      reinterpret_cast<Sc(*)[kTileSpStride]>(smem_raw + kTileSidxBytes + kTileScoreBytes);
+  // dp per (pair, slot), then dS * scale in place
+  float(*sdp)[kTileIdxStride] =
+      reinterpret_cast<float(*)[kTileIdxStride]>(smem_raw + kTileSidxBytes + kTileScoreBytes);
   const int w = p.pat.w;
   const int n = p.n_rows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -481,15 +517,18 @@ bwd_query_tile_kernel(const AttnParams p) {
   const int my_j = j0 + my_pi / G;
   const int my_h = hkv * G + my_pi % G;
   const bool my_live = my_j < n;
+  // lane r of a group reads chunks r, r + LPR, ... of a row
   const T* Kb = reinterpret_cast<const T*>(p.k) + b * p.skb + hkv * p.skh + r * EPL;
   const T* Vb = reinterpret_cast<const T*>(p.v) + b * p.svb + hkv * p.svh + r * EPL;
-  auto row_of = [&](const void* base, int64_t sb, int64_t sh, int64_t ss, int m) -> uint4 {
+  // the CPL chunks of this lane of row j of pair m's head in a [B, Hq, n, D] tensor
+  auto row_of = [&](const void* base, int64_t sb, int64_t sh, int64_t ss, int m, uint4 (&out)[CPL]) {
     const int pi = pw0 + m * RPW + g;
     const int j = j0 + pi / G;
     const int h = hkv * G + pi % G;
-    return j < n ? ldg16_stream(reinterpret_cast<const T*>(base) + b * sb + h * sh +
-                                (int64_t)j * ss + r * EPL)
-                 : make_uint4(0, 0, 0, 0);
+    const T* row = reinterpret_cast<const T*>(base) + b * sb + h * sh + (int64_t)j * ss + r * EPL;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c)
+      out[c] = j < n ? ldg16_stream(row + c * LPR * EPL) : make_uint4(0, 0, 0, 0);
   };
 
   // ---- pass 1a: p = exp2(s * scale_log2 - lse), or the forward's p --------
@@ -507,9 +546,9 @@ bwd_query_tile_kernel(const AttnParams p) {
     __syncthreads();
   } else {
     const float lse2 = my_live ? p.lse[((int64_t)b * p.Hq + my_h) * n + my_j] : 0.f;
-    uint4 qv[MI];
+    uint4 qv[MI][CPL];
 #pragma unroll
-    for (int m = 0; m < MI; ++m) qv[m] = row_of(p.q, p.sqb, p.sqh, p.sqs, m);
+    for (int m = 0; m < MI; ++m) row_of(p.q, p.sqb, p.sqh, p.sqs, m, qv[m]);
     for (int k0 = 0; k0 < w; k0 += 2) {
       int2 rows[MI];
 #pragma unroll
@@ -517,12 +556,20 @@ bwd_query_tile_kernel(const AttnParams p) {
       float part[LPR];
 #pragma unroll
       for (int s2 = 0; s2 < 2; ++s2) {
-        uint4 kb[MI];
+        uint4 kb[MI][CPL];
 #pragma unroll
-        for (int m = 0; m < MI; ++m)
-          kb[m] = ldg16(Kb + (int64_t)(row2_at(rows[m], s2) & kRowMask) * p.sks);
+        for (int m = 0; m < MI; ++m) {
+          const T* krow = Kb + (int64_t)(row2_at(rows[m], s2) & kRowMask) * p.sks;
 #pragma unroll
-        for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(qv[m], kb[m], 0.f);
+          for (int c = 0; c < CPL; ++c) kb[m][c] = ldg16(krow + c * LPR * EPL);
+        }
+#pragma unroll
+        for (int m = 0; m < MI; ++m) {
+          float d = 0.f;
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) d = M::dot(qv[m][c], kb[m][c], d);
+          part[s2 * MI + m] = d;
+        }
       }
       transpose_reduce<LPR>(part, lane);
       const int k = k0 + r / MI;
@@ -530,21 +577,12 @@ bwd_query_tile_kernel(const AttnParams p) {
     }
   }
 
-  // ---- pass 1b: dp, dS, workspace ------------------------------------------
+  // ---- pass 1b: dp = dO.v and delta = sum_k p_k dp_k ---------------------
   {
-    uint4 dv[MI];
-    float delta[MI];
+    uint4 dv[MI][CPL];
 #pragma unroll
-    for (int m = 0; m < MI; ++m) {
-      dv[m] = row_of(p.dout, p.sdob, p.sdoh, p.sdos, m);
-      delta[m] = group_allreduce_sum<LPR>(M::dot(dv[m], row_of(p.o, p.sob, p.soh, p.sos, m), 0.f));
-    }
-    // delta of the pair this lane ends with: pair pw0 + (r % MI) * RPW + g
-    float my_delta = 0.f;
-#pragma unroll
-    for (int m = 0; m < MI; ++m) my_delta = (r % MI) == m ? delta[m] : my_delta;
-    float2* pds_pair = p.pds + ((int64_t)(b * p.Hq + my_h) * w) * n + my_j;
-    const uint64_t pol_ws = l2_evict_first_policy();   // read once, by the key side
+    for (int m = 0; m < MI; ++m) row_of(p.dout, p.sdob, p.sdoh, p.sdos, m, dv[m]);
+    float dpart = 0.f;   // this lane's slots of pair my_pi
     for (int k0 = 0; k0 < w; k0 += 2) {
       int2 rows[MI];
 #pragma unroll
@@ -552,46 +590,74 @@ bwd_query_tile_kernel(const AttnParams p) {
       float part[LPR];
 #pragma unroll
       for (int s2 = 0; s2 < 2; ++s2) {
-        uint4 vb[MI];
+        uint4 vb[MI][CPL];
 #pragma unroll
-        for (int m = 0; m < MI; ++m)
-          vb[m] = ldg16(Vb + (int64_t)(row2_at(rows[m], s2) & kRowMask) * p.svs);
+        for (int m = 0; m < MI; ++m) {
+          const T* vrow = Vb + (int64_t)(row2_at(rows[m], s2) & kRowMask) * p.svs;
 #pragma unroll
-        for (int m = 0; m < MI; ++m) part[s2 * MI + m] = M::dot(dv[m], vb[m], 0.f);
+          for (int c = 0; c < CPL; ++c) vb[m][c] = ldg16(vrow + c * LPR * EPL);
+        }
+#pragma unroll
+        for (int m = 0; m < MI; ++m) {
+          float d = 0.f;
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) d = M::dot(dv[m][c], vb[m][c], d);
+          part[s2 * MI + m] = d;
+        }
       }
       transpose_reduce<LPR>(part, lane);
       const int k = k0 + r / MI;
-      // a slot past w (odd w) gets p = dS = 0: pass 2 reads it
+      // a slot past w (odd w) and masked slots have p = 0
       const float pk = k < w ? sprob[my_pi][k] : 0.f;
-      const float dsk = pk * (part[0] - my_delta) * p.scale;   // 0 for masked slots
+      sdp[my_pi][k] = part[0];
+      dpart += pk * part[0];
+    }
+    // lanes r and r ^ MI hold the even / odd slots of the same pair
+    const float delta = dpart + __shfl_xor_sync(0xffffffffu, dpart, MI);
+    // dS = p (dp - delta), the (p, dS * scale) workspace, dS * scale in place of dp
+    float2* pds_pair = p.pds + ((int64_t)(b * p.Hq + my_h) * w) * n + my_j;
+    const uint64_t pol_ws = l2_evict_first_policy();   // read once, by the key side
+    for (int k = r / MI; k < w + 1; k += 2) {
+      if (k >= kTileMaxW) break;
+      const float pk = k < w ? sprob[my_pi][k] : 0.f;
+      const float dsk = pk * (sdp[my_pi][k] - delta) * p.scale;   // 0 for masked slots
       if (my_live && k < w) stg_f2_hint(pds_pair + (int64_t)k * n, make_float2(pk, dsk), pol_ws);
-      sds[my_pi][k] = M::scalar(dsk);
+      sdp[my_pi][k] = dsk;
     }
   }
   __syncthreads();
 
   // ---- pass 2: dQ = sum dS k ------------------------------------------------
-  float acc[MI][EPL];
+  float acc[MI][CPL * EPL];
 #pragma unroll
   for (int m = 0; m < MI; ++m)
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) acc[m][e] = 0.f;
+    for (int e = 0; e < CPL * EPL; ++e) acc[m][e] = 0.f;
+  // dS * scale of 2 slots per shared load (fp32, rounded to the input type
+  // for the mixed-precision FMA); a slot past w (odd w) has dS = 0
   for (int k0 = 0; k0 < w; k0 += 2) {
     int2 rows[MI];
-    uint32_t wts[MI];
+    float2 wts[MI];
 #pragma unroll
     for (int m = 0; m < MI; ++m) {
       rows[m] = slot_rows2(sidx, pw0 + m * RPW + g, k0);
-      wts[m] = weights2(&sds[pw0 + m * RPW + g][0], k0);
+      wts[m] = make_float2(sdp[pw0 + m * RPW + g][k0], sdp[pw0 + m * RPW + g][k0 + 1]);
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      uint4 kb[MI];
+      uint4 kb[MI][CPL];
 #pragma unroll
-      for (int m = 0; m < MI; ++m)
-        kb[m] = ldg16(Kb + (int64_t)(row2_at(rows[m], i) & kRowMask) * p.sks);
+      for (int m = 0; m < MI; ++m) {
+        const T* krow = Kb + (int64_t)(row2_at(rows[m], i) & kRowMask) * p.sks;
 #pragma unroll
-      for (int m = 0; m < MI; ++m) M::axpy(weight2_at(wts[m], i), kb[m], acc[m]);
+        for (int c = 0; c < CPL; ++c) kb[m][c] = ldg16(krow + c * LPR * EPL);
+      }
+#pragma unroll
+      for (int m = 0; m < MI; ++m) {
+        const Sc wt = M::scalar(i ? wts[m].y : wts[m].x);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) M::axpy(wt, kb[m][c], acc[m] + c * EPL);
+      }
     }
   }
 #pragma unroll
@@ -601,7 +667,8 @@ bwd_query_tile_kernel(const AttnParams p) {
     const int h = hkv * G + pi % G;
     if (j < n) {
       T* dqrow = reinterpret_cast<T*>(p.dq) + b * p.sdqb + h * p.sdqh + (int64_t)j * p.sdqs + r * EPL;
-      stg16(dqrow, V::from_float(acc[m]));
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) stg16(dqrow + c * LPR * EPL, V::from_float(acc[m] + c * EPL));
     }
   }
 }
@@ -623,7 +690,10 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
   const int wpad = (w + 31) & ~31;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* sidx = reinterpret_cast<int*>(smem_raw) + warp * 3 * wpad;
-  Sc* sds = reinterpret_cast<Sc*>(sidx + wpad);   // dS * scale in the input type
+  // per slot: p (the sign bit set when dropout drops the slot), and dP (after
+  // dropout), then dS * scale in its place
+  float* spk = reinterpret_cast<float*>(sidx + wpad);
+  float* sdp = spk + wpad;
   const int g = lane / LPR, r = lane % LPR;
   const int hkv = blockIdx.y, b = blockIdx.z;
   const int row0 = blockIdx.x * rows_per_cta;
@@ -640,21 +710,18 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
     fill_slot_rows(p, pos, h, wpad, lane, sidx);
 
     uint4 qv, dv;
-    float delta;
     {
       const int64_t jr = (int64_t)j;
       const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.sqb + h * p.sqh + jr * p.sqs + r * EPL;
       const T* drow = reinterpret_cast<const T*>(p.dout) + b * p.sdob + h * p.sdoh + jr * p.sdos + r * EPL;
-      const T* orow = reinterpret_cast<const T*>(p.o) + b * p.sob + h * p.soh + jr * p.sos + r * EPL;
       qv = ldg16_stream(qrow);
       dv = ldg16_stream(drow);
-      // rowsum(dO * O), every group holds it
-      delta = group_allreduce_sum<LPR>(M::dot(dv, ldg16_stream(orow), 0.f));
     }
     const float lse2 = p.lse[((int64_t)b * p.Hq + h) * n + j];
     float2* pds_row = p.pds + ((int64_t)(b * p.Hq + h) * w) * n + j;
     __syncwarp();
 
+    float dpart = 0.f;
     for (int s0 = 0; s0 < wpad; s0 += 32) {
       float ps[LPR], pp[LPR];
       {
@@ -680,23 +747,33 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
       transpose_reduce<LPR>(ps, lane);
       transpose_reduce<LPR>(pp, lane);
       const int k = s0 + r * RPW + g;
-      float pk = 0.f, dsk = 0.f;
+      float pk = 0.f, dpk = 0.f;
+      bool keep = true;
       if (sidx[k] >= 0) {
         pk = exp2f(ps[0] * p.scale_log2 - lse2);
-        float dpk = pp[0];
+        dpk = pp[0];
         if (p.drop_threshold) {
           // the same keep mask as the forward: dP = mask / (1 - p) * dO.v and
           // the weight used for dV is the kept, rescaled one
-          const bool keep = dropout_keep(p, pos, b, h, k);
+          keep = dropout_keep(p, pos, b, h, k);
           dpk = keep ? dpk * p.keep_scale : 0.f;
-          dsk = pk * (dpk - delta) * p.scale;
-          pk = keep ? pk * p.keep_scale : 0.f;
-        } else {
-          dsk = pk * (dpk - delta) * p.scale;
         }
       }
-      if (k < w) pds_row[(int64_t)k * n] = make_float2(pk, dsk);
-      sds[k] = M::scalar(dsk);
+      spk[k] = keep ? pk : -pk;
+      sdp[k] = dpk;
+      dpart += pk * dpk;
+    }
+    // delta = sum_k p_k dP_k = rowsum(dO o O) for the exact O (with dropout:
+    // the O of the kept, rescaled weights), without the stored O's rounding
+    const float delta = warp_sum(dpart);
+    __syncwarp();
+    for (int k = lane; k < wpad; k += 32) {
+      const float v = spk[k];
+      const float pk = fabsf(v);
+      const float dsk = pk * (sdp[k] - delta) * p.scale;   // 0 for masked slots
+      const float pw = signbit(v) ? 0.f : (p.drop_threshold ? pk * p.keep_scale : pk);
+      if (k < w) pds_row[(int64_t)k * n] = make_float2(pw, dsk);
+      sdp[k] = dsk;
     }
     __syncwarp();
 
@@ -711,7 +788,7 @@ bwd_query_kernel(const AttnParams p, int rows_per_cta) {
         kb[m] = row >= 0 ? ldg16(Kb + (int64_t)row * p.sks) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int m = 0; m < LPR; ++m) M::axpy(sds[s0 + m * RPW + g], kb[m], acc);   // 0 when masked
+      for (int m = 0; m < LPR; ++m) M::axpy(M::scalar(sdp[s0 + m * RPW + g]), kb[m], acc);   // 0 when masked
     }
 #pragma unroll
     for (int o = LPR; o < 32; o <<= 1)

@@ -60,15 +60,18 @@ gather_probe_kernel(const AttnParams p, uint32_t* sink) {
                        : 0;
   // rows of 2 slots of pair pi (a slot past w: the masked in-bounds row)
   auto rows_at = [&](int pi, int k0) -> int2 {
-    if (MODE == kProbePattern) return slot_rows2(sidx, pi, k0);
-    int v[2];
+    if constexpr (MODE == kProbePattern) {
+      return slot_rows2(sidx, pi, k0);
+    } else {
+      int v[2];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const uint32_t hsh = probe_mix(cta * 8192u + (uint32_t)(pi * kTileMaxW + k0 + i));
-      v[i] = MODE == kProbeL2Random ? (int)(hsh % (uint32_t)p.kv_rows)
-                                    : win0 + (int)(hsh & (kProbeWindowRows - 1));
+      for (int i = 0; i < 2; ++i) {
+        const uint32_t hsh = probe_mix(cta * 8192u + (uint32_t)(pi * kTileMaxW + k0 + i));
+        v[i] = MODE == kProbeL2Random ? (int)(hsh % (uint32_t)p.kv_rows)
+                                      : win0 + (int)(hsh & (kProbeWindowRows - 1));
+      }
+      return make_int2(v[0], v[1]);
     }
-    return make_int2(v[0], v[1]);
   };
   const int pw0 = warp * PPW;
   const T* Kb = reinterpret_cast<const T*>(p.k) + b * p.skb + hkv * p.skh + r * EPL;
