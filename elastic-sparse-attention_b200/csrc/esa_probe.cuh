@@ -4,10 +4,11 @@
 //
 // Same grid, CTA shape and load order as fwd_tile_kernel: a CTA owns 128
 // (query, head) pairs of one KV head (128 / G queries x G heads), warp w owns
-// pairs [16w, 16w + 16), half a warp load is one 256-byte row; all warps walk
-// the slots together, K rows first (the score pass), then V rows (the P V
-// pass), two slots per step with their rows in one shared load.  The
-// rows come from the elastic pattern (the
+// pairs [16w, 16w + 16), 8 lanes read a row (D / 64 16-byte chunks each, so
+// one warp load covers 4 rows); all warps walk the slots together, K rows
+// first (the score pass), then V rows (the P V pass), two slots per step
+// with their rows in one shared load.  The rows come from the elastic
+// pattern (the
 // tile kernels' exact stream), uniformly at random over the KV head's rows
 // (an L2-resident random gather), or at random within 64 rows per CTA (an
 // L1-resident gather).  The loaded words are folded into an xor checksum
@@ -33,8 +34,8 @@ __device__ __forceinline__ uint32_t probe_mix(uint32_t x) {
 template <typename T, int D, int MODE>
 __global__ void __launch_bounds__(256, 2)
 gather_probe_kernel(const AttnParams p, uint32_t* sink) {
-  using L = Layout<T, D>;
-  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW;
+  using L = TileLayout<T, D>;
+  constexpr int EPL = L::EPL, LPR = L::LPR, RPW = L::RPW, CPL = L::CPL;
   constexpr int PPW = kTilePairs / 8;      // pairs per warp
   constexpr int MI = PPW / RPW;            // warp loads per slot
   constexpr int HALF = kTileMaxW / 2;
@@ -85,16 +86,20 @@ gather_probe_kernel(const AttnParams p, uint32_t* sink) {
       int2 rows[MI];
 #pragma unroll
       for (int m = 0; m < MI; ++m) rows[m] = rows_at(pw0 + m * RPW + g, k0);
-      uint4 x[2][MI];
 #pragma unroll
-      for (int s2 = 0; s2 < 2; ++s2)
+      for (int s2 = 0; s2 < 2; ++s2) {
+        uint4 x[MI][CPL];
+#pragma unroll
+        for (int m = 0; m < MI; ++m) {
+          const T* row = base + (int64_t)(row2_at(rows[m], s2) & kRowMask) * stride;
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) x[m][c] = ldg16(row + c * LPR * EPL);
+        }
 #pragma unroll
         for (int m = 0; m < MI; ++m)
-          x[s2][m] = ldg16(base + (int64_t)(row2_at(rows[m], s2) & kRowMask) * stride);
 #pragma unroll
-      for (int s2 = 0; s2 < 2; ++s2)
-#pragma unroll
-        for (int m = 0; m < MI; ++m) acc ^= x[s2][m].x ^ x[s2][m].y ^ x[s2][m].z ^ x[s2][m].w;
+          for (int c = 0; c < CPL; ++c) acc ^= x[m][c].x ^ x[m][c].y ^ x[m][c].z ^ x[m][c].w;
+      }
     }
   }
   if (acc == 0x9E3779B9u) *sink = acc;

@@ -135,6 +135,51 @@ __device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Split form of tmem_ld_x32 for several loads in flight: tmem_ld_x32_issue
+// starts a load, tmem_ld_wait waits for every load this thread started, and
+// reg_fence32 (one per issued load, after the wait) makes the loaded registers
+// depend on a statement that follows the wait, so no use of them can be
+// scheduled before it (volatile asm statements keep their order).
+__device__ __forceinline__ void tmem_ld_x32_issue(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void reg_fence32(uint32_t* r) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31]));
+}
+// NC x 32 consecutive fp32 columns of this warp's 32 TMEM lanes, one wait.
+template <int NC>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
+  uint32_t r[NC][32];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) tmem_ld_x32_issue(taddr + c * 32, r[c]);
+  tmem_ld_wait();
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    reg_fence32(r[c]);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(r[c][i]);
+  }
+}
+
 // ---- descriptors -------------------------------------------------------------
 // Shared-memory matrix descriptor, 128-byte swizzle (operand tile base must be
 // 1024-byte aligned).  lbo/sbo in bytes.

@@ -252,39 +252,40 @@ window_fwd_tc_kernel(const __grid_constant__ WindowTmaps maps, const AttnParams 
       sm100::tc_fence_after();
       float mx = -INFINITY, l = 0.f;
       if (ok) {
-        // two passes over the TMEM row, 32 columns at a time: the maximum,
-        // then P (TMEM reads are cheap; a whole row in registers would spill)
-        const int nch = (nk + 31) / 32;
-        for (int c = 0; c < nch; ++c) {
-          float sc[32];
-          sm100::tmem_ld_x32(tmem + s * 256 + lane_base + c * 32, sc);
+        // the maximum over the whole S row (kWinMaxKeys columns of the stage,
+        // those past nk masked) with one TMEM wait; then P from two reloads of
+        // half the row (a whole row held across the exponentials would spill)
+        {
+          float sc[kWinMaxKeys];
+          sm100::tmem_ld_cols<kWinMaxKeys / 32>(tmem + s * 256 + lane_base, sc);
 #pragma unroll
-          for (int u = 0; u < 32; ++u) {
-            const int col = c * 32 + u;
-            if (col < nk && col >= lo && col <= hi) mx = fmaxf(mx, sc[u] * p.scale_log2);
-          }
+          for (int col = 0; col < kWinMaxKeys; ++col)
+            if (col < nk && col >= lo && col <= hi) mx = fmaxf(mx, sc[col] * p.scale_log2);
         }
         const float m = mx == -INFINITY ? 0.f : mx;
         // P row over the tile's Q: K-major, 128B swizzle, 64 keys per chunk
-        for (int c = 0; c < nch; ++c) {
-          float sc[32];
-          sm100::tmem_ld_x32(tmem + s * 256 + lane_base + c * 32, sc);
 #pragma unroll
-          for (int u8 = 0; u8 < 4; ++u8) {
-            const int c8 = c * 4 + u8;
-            if (c8 * 8 < nk) {
-              float e[8];
+        for (int hf = 0; hf < kWinMaxKeys / 64; ++hf) {
+          if (hf * 64 < nk) {
+            float sc[64];
+            sm100::tmem_ld_cols<2>(tmem + s * 256 + lane_base + hf * 64, sc);
 #pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                const int col = c8 * 8 + u;
-                const bool valid = col >= lo && col <= hi;
-                e[u] = valid ? exp2f(sc[u8 * 8 + u] * p.scale_log2 - m) : 0.f;
-                l += e[u];
+            for (int u8 = 0; u8 < 8; ++u8) {
+              const int c8 = hf * 8 + u8;
+              if (c8 * 8 < nk) {
+                float e[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  const int col = c8 * 8 + u;
+                  const bool valid = col >= lo && col <= hi;
+                  e[u] = valid ? exp2f(sc[u8 * 8 + u] * p.scale_log2 - m) : 0.f;
+                  l += e[u];
+                }
+                const int chunk = c8 >> 3, unit = c8 & 7;
+                unsigned char* dst =
+                    sQ(s) + chunk * (kWinRows * 128) + t * 128 + ((unit ^ (t & 7)) << 4);
+                *reinterpret_cast<uint4*>(dst) = Vec<T>::from_float(e);
               }
-              const int chunk = c8 >> 3, unit = c8 & 7;
-              unsigned char* dst =
-                  sQ(s) + chunk * (kWinRows * 128) + t * 128 + ((unit ^ (t & 7)) << 4);
-              *reinterpret_cast<uint4*>(dst) = Vec<T>::from_float(e);
             }
           }
         }
@@ -305,14 +306,14 @@ window_fwd_tc_kernel(const __grid_constant__ WindowTmaps maps, const AttnParams 
         const float inv = l > 0.f ? 1.f / l : 0.f;
         T* orow = reinterpret_cast<T*>(p.o) + tl.b * p.sob + h * p.soh + (int64_t)j * p.sos;
 #pragma unroll
-        for (int c = 0; c < kWinHeadDim / 32; ++c) {
-          float o[32];
-          sm100::tmem_ld_x32(tmem + s * 256 + 128 + lane_base + c * 32, o);
+        for (int hf = 0; hf < kWinHeadDim / 64; ++hf) {
+          float o[64];
+          sm100::tmem_ld_cols<2>(tmem + s * 256 + 128 + lane_base + hf * 64, o);
 #pragma unroll
-          for (int u = 0; u < 32; ++u) o[u] *= inv;
+          for (int u = 0; u < 64; ++u) o[u] *= inv;
           if (store) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) stg16(orow + c * 32 + u * 8, Vec<T>::from_float(o + u * 8));
+            for (int u = 0; u < 8; ++u) stg16(orow + hf * 64 + u * 8, Vec<T>::from_float(o + u * 8));
           }
         }
         if (store) p.lse[((int64_t)tl.b * p.Hq + h) * p.n_rows + j] = mx + log2f(l);
