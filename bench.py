@@ -197,7 +197,7 @@ FAMILY = {"window_fwd_tc": "fwd_window", "fwd_tile": "fwd_tile", "fwd_gather": "
           "fwd_decode": "fwd_decode", "window_bwd_dq_tc": "bwd_window",
           "window_bwd_dkv_tc": "bwd_window", "bwd_query_tile": "bwd_query",
           "bwd_query": "bwd_query", "bwd_heavy": "bwd_heavy", "bwd_key_mma": "bwd_key",
-          "bwd_key": "bwd_key"}
+          "bwd_key_plan": "bwd_key", "bwd_key": "bwd_key"}
 
 
 def layer_bytes(nh, nkv, n=L, es=ES):
@@ -252,7 +252,8 @@ def trace_step(esa, fn):
 def gather_probes(esa, q, k, v, spec, reps=3):
     """Row-gather ceilings on this problem (esa_probe_gather): the tile
     kernels' exact row stream, uniformly random rows of a KV head (L2), random
-    rows within 64 per CTA (L1); GB/s of 256-byte rows (K and V)."""
+    rows within 64 per CTA (L1), runs of consecutive rows read once per CTA
+    (L2 streaming, the key side's access); GB/s of 256-byte rows (K and V)."""
     import ctypes
     lib = esa._lib.load()
     sink = torch.zeros(4, dtype=torch.int32, device=q.device)
@@ -261,7 +262,7 @@ def gather_probes(esa, q, k, v, spec, reps=3):
     nbytes = units * 2 * D * ES
     stream = torch.cuda.current_stream()
     out = {}
-    for mode, name in ((0, "pattern"), (1, "l2_random"), (2, "l1_window")):
+    for mode, name in ((0, "pattern"), (1, "l2_random"), (2, "l1_window"), (3, "l2_stream")):
         def run():
             esa._lib.check(lib.esa_probe_gather(mode, ctypes.byref(pb), esa._lib.tensor4(k),
                                                 esa._lib.tensor4(v), sink.data_ptr(),
@@ -317,11 +318,15 @@ def bench_ours(args, world, rank, local):
     for layer in range(NL):   # one-time pattern audit (backward precondition), outside timing
         assert esa.ops.pattern_audit(HQ, esa.PatternSpec(layer, NL, W), L, dev) == 0
     probs = [esa.ops.probs_buffer(q, k, s) for s in specs]
+    # the key side's plans, built once per layer like the module does at its
+    # first backward (pattern-only data, outside timing)
+    plans = [esa.ops.key_plan(q, k, s) for s in specs]
+    plan_bytes = sum(p.numel() for p in plans if p is not None)
 
     def step():
-        for s, pr in zip(specs, probs):
+        for s, pr, kp in zip(specs, probs, plans):
             o, lse = esa.ops.forward(q, k, v, s, scale, probs=pr)
-            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws, probs=pr)
+            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws, probs=pr, key_plan=kp)
 
     ms, clocks = timed_steps(step, args.steps, args.warmup, dev, world)
 
@@ -422,7 +427,9 @@ def bench_ours(args, world, rank, local):
                    "num_hidden_layers": NL,
                    "parallelism": (f"head split x{world}: {nkv} KV heads ({nh} query heads) per "
                                    "rank, no collective" if world > 1 else "1 GPU"),
-                   "l2": "inputs 2.7 GB > 126 MB L2, no flush"},
+                   "l2": "inputs 2.7 GB > 126 MB L2, no flush",
+                   "key_plans": f"{plan_bytes / 1e9:.2f} GB of precomputed key-side user "
+                                "lists (pattern-only, built once per layer outside timing)"},
         "value_note": "dense-equivalent count over touched 128x128 blocks (the north-star "
                       "definition); can exceed the dense peak; see useful_tflops",
         "useful_tflops": round(useful, 2),
@@ -540,15 +547,16 @@ def bench_weak(esa, args, dev, world):
     ws = torch.empty(esa.ops.backward_workspace_bytes(q, k, specs[0]), dtype=torch.uint8,
                      device=dev)
     probs = [esa.ops.probs_buffer(q, k, s) for s in specs]
+    plans = [esa.ops.key_plan(q, k, s) for s in specs]
 
     def step():
-        for s, pr in zip(specs, probs):
+        for s, pr, kp in zip(specs, probs, plans):
             o, lse = esa.ops.forward(q, k, v, s, scale, probs=pr)
-            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws, probs=pr)
+            esa.ops.backward(q, k, v, o, lse, do, s, scale, workspace=ws, probs=pr, key_plan=kp)
 
     ms, _ = timed_steps(step, 3, 2, dev, world)
     eff = sum(3.5 * 4 * D * TILE * TILE * a for a in ACTIVE_BLOCKS_C3) * B
-    del q, k, v, do, ws, probs
+    del q, k, v, do, ws, probs, plans
     torch.cuda.empty_cache()
     return {"value": round(eff * world / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
             "ms_per_step": round(ms, 3), "global_batch": world, "steps": 3,
@@ -1021,10 +1029,11 @@ def profile_case(args):
     v = torch.randn(B, hkv, n, D, device=dev, generator=g).to(torch.bfloat16)
     do = torch.randn(B, hq, n, D, device=dev, generator=g).to(torch.bfloat16)
     spec = esa.PatternSpec(args.layer, NL, W)
+    plan = esa.ops.key_plan(q, k, spec) if args.key_plan else None
     for _ in range(args.steps):
         pr = esa.ops.probs_buffer(q, k, spec)
         o, lse = esa.ops.forward(q, k, v, spec, D ** -0.5, probs=pr)
-        esa.ops.backward(q, k, v, o, lse, do, spec, D ** -0.5, probs=pr)
+        esa.ops.backward(q, k, v, o, lse, do, spec, D ** -0.5, probs=pr, key_plan=plan)
     torch.cuda.synchronize()
     print(json.dumps({"case": "one-layer", "seq_len": n, "layer": args.layer, "heads": hq,
                       "out_mean_abs": float(o.float().abs().mean())}))
@@ -1044,6 +1053,8 @@ def main():
     ap.add_argument("--seq-len", type=int, default=32768)
     ap.add_argument("--layer", type=int, default=5)
     ap.add_argument("--heads", type=int, default=HQ, help="one-layer: query heads (GQA 4:1)")
+    ap.add_argument("--key-plan", action="store_true",
+                    help="one-layer: give the backward the layer's key plan")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)

@@ -6,13 +6,13 @@ HighCWu/elastic-sparse-attention.  Import it as ``elastic_sparse_attention_b200`
 directory).
 """
 from . import _lib, layer_ops, ops
-from .attention import ElasticSparseAttention, ElasticSparseAttentionFunction
+from .attention import ElasticSparseAttention, ElasticSparseAttentionFunction, KeyPlanCache
 from .decoder import ElasticDecoderStack
 from .head_split import HeadShardedElasticSparseAttention, head_share
 from .ops import PatternSpec
 from .sharded import SequenceShardedElasticSparseAttention
 
 __all__ = ["ElasticSparseAttention", "ElasticSparseAttentionFunction", "ElasticDecoderStack",
-           "HeadShardedElasticSparseAttention", "PatternSpec",
+           "HeadShardedElasticSparseAttention", "KeyPlanCache", "PatternSpec",
            "SequenceShardedElasticSparseAttention", "head_share", "layer_ops", "ops", "_lib"]
-__version__ = "0.1.0"
+__version__ = "0.1.2"

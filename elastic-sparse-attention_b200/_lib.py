@@ -24,6 +24,7 @@ DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 EXPORTED = ("esa_version", "esa_last_error", "esa_device_errors", "esa_forward_writes_probs",
             "esa_pattern",
             "esa_pattern_audit", "esa_forward", "esa_backward_workspace_size", "esa_backward",
+            "esa_key_plan_size", "esa_key_plan_build",
             "esa_backward_noalloc", "esa_trace_enable", "esa_trace_count", "esa_trace_read",
             "esa_probe_gather",
             # decoder-layer harness (include/esa_layer.h)
@@ -34,6 +35,7 @@ EXPORTED = ("esa_version", "esa_last_error", "esa_device_errors", "esa_forward_w
 DEVERR_KV_RANGE = 1
 DEVERR_TIMEOUT = 2
 DEVERR_QUERY_RANGE = 4
+DEVERR_PLAN = 8
 
 
 class EsaTensor(ctypes.Structure):
@@ -53,7 +55,8 @@ class EsaProblem(ctypes.Structure):
                 ("dropout_p", ctypes.c_float), ("head_offset", ctypes.c_int32),
                 ("dropout_seed", ctypes.c_uint64), ("weights", ctypes.c_void_p),
                 ("probs", ctypes.c_void_p), ("pattern_heads", ctypes.c_int32),
-                ("reserved", ctypes.c_int32)]
+                ("reserved", ctypes.c_int32), ("key_plan", ctypes.c_void_p),
+                ("key_plan_bytes", ctypes.c_uint64)]
 
 
 class EsaError(RuntimeError):
@@ -99,6 +102,10 @@ def load() -> ctypes.CDLL:
                                      EsaTensor, P, EsaTensor, EsaTensor, EsaTensor, EsaTensor,
                                      P, P, P, ctypes.c_size_t, P]
         lib.esa_backward.restype = ctypes.c_int
+        lib.esa_key_plan_size.argtypes = [ctypes.POINTER(EsaProblem)]
+        lib.esa_key_plan_size.restype = ctypes.c_size_t
+        lib.esa_key_plan_build.argtypes = [ctypes.POINTER(EsaProblem), P, ctypes.c_size_t, P]
+        lib.esa_key_plan_build.restype = ctypes.c_int
         lib.esa_trace_enable.argtypes = [i32]
         lib.esa_trace_enable.restype = ctypes.c_int
         lib.esa_trace_count.restype = ctypes.c_int
@@ -155,14 +162,15 @@ def problem(*, dtype: torch.dtype, batch: int, num_heads: int, num_kv_heads: int
             dropout_p: float = 0.0, dropout_seed: int = 0,
             weights: torch.Tensor | None = None,
             probs: torch.Tensor | None = None, head_offset: int = 0,
-            pattern_heads: int = 0) -> EsaProblem:
+            pattern_heads: int = 0, key_plan: torch.Tensor | None = None) -> EsaProblem:
     if dtype not in DTYPES:
         raise TypeError(f"unsupported dtype {dtype}; expected float32, bfloat16 or float16")
     return EsaProblem(DTYPES[dtype], batch, num_heads, num_kv_heads, head_dim, attn_length,
                       layer_idx, num_hidden_layers, q_len, kv_len, kv_offset,
                       kv_len if kv_rows is None else kv_rows, row_offset, ptr(rows), scale, flags,
                       dropout_p, head_offset, dropout_seed, ptr(weights), ptr(probs),
-                      pattern_heads, 0)
+                      pattern_heads, 0, ptr(key_plan),
+                      0 if key_plan is None else key_plan.numel())
 
 
 def trace_records() -> list[tuple[str, float]]:

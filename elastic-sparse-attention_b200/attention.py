@@ -61,19 +61,46 @@ def _ensure_monotone(num_heads: int, spec: PatternSpec, seq_len: int, device: to
         _audited[key] = max(_audited.get(key, 0), seq_len)
 
 
+class KeyPlanCache:
+    """The key plan (:func:`ops.key_plan`) of one layer, built at the first
+    backward of a shape and kept while the shape repeats, like the reference
+    module keeps its index buffers (:454-468).  One plan is held at a time: a
+    call with other shapes replaces it."""
+
+    def __init__(self, enabled: bool = True):
+        self.enabled = enabled
+        self._key = None
+        self._plan = None
+
+    def get(self, q: torch.Tensor, k: torch.Tensor, spec: PatternSpec) -> Optional[torch.Tensor]:
+        if not self.enabled:
+            return None
+        key = (q.device, q.dtype, tuple(q.shape[1:]), tuple(k.shape[1:3]), spec)
+        if key != self._key:
+            self._key, self._plan = None, None   # release the old plan first
+            self._plan = ops.key_plan(q, k, spec)
+            self._key = key
+        return self._plan
+
+    def clear(self) -> None:
+        self._key, self._plan = None, None
+
+
 class ElasticSparseAttentionFunction(torch.autograd.Function):
     """Autograd boundary (reference ``ElasticSparseAttentionFunction``, :235-339).
 
     ``apply(q, k, v, pattern, sm_scale, num_kv_groups, rows=None)``: instead of
     materialised ``sparse_indices`` / ``sparse_mask`` tensors, ``pattern`` is the
     :class:`PatternSpec` they are generated from and ``rows`` the optional query
-    positions (``cache_position``).  Returns o ``[B, H, q_len, D]``.
+    positions (``cache_position``).  ``plans`` (a :class:`KeyPlanCache`)
+    supplies the backward's key plan.  Returns o ``[B, H, q_len, D]``.
     """
 
     @staticmethod
     def forward(ctx, q, k, v, pattern: PatternSpec, sm_scale: float, num_kv_groups: int,
                 rows: Optional[torch.Tensor] = None, dropout_p: float = 0.0,
-                dropout_seed: int = 0, return_weights: bool = False):
+                dropout_seed: int = 0, return_weights: bool = False,
+                plans: Optional[KeyPlanCache] = None):
         if q.shape[1] != k.shape[1] * num_kv_groups:
             raise ValueError("num_kv_groups does not match the query / key head counts")
         q, k, v = (ops.as_kernel_operand(t) for t in (q, k, v))
@@ -87,6 +114,7 @@ class ElasticSparseAttentionFunction(torch.autograd.Function):
         ctx.pattern = pattern
         ctx.sm_scale = sm_scale
         ctx.dropout = (dropout_p, dropout_seed)
+        ctx.plans = plans
         if return_weights:
             ctx.mark_non_differentiable(res[2])
             return o, res[2]
@@ -104,11 +132,12 @@ class ElasticSparseAttentionFunction(torch.autograd.Function):
         else:
             seq = q.shape[2]
         _ensure_monotone(q.shape[1], spec, max(seq, 2), q.device)
+        plan = ctx.plans.get(q, k, spec) if ctx.plans is not None and rows is None else None
         dq, dk, dv = ops.backward(q, k, v, o, lse, do, spec, ctx.sm_scale, rows=rows,
                                   sorted_rows=sorted_rows, row_perm=perm,
                                   dropout_p=ctx.dropout[0], dropout_seed=ctx.dropout[1],
-                                  probs=probs)
-        return dq, dk, dv, None, None, None, None, None, None, None
+                                  probs=probs, key_plan=plan)
+        return dq, dk, dv, None, None, None, None, None, None, None, None
 
 
 def _forward_without_grad(q, k, v, pattern: PatternSpec, sm_scale: float, num_kv_groups: int,
@@ -167,6 +196,10 @@ class ElasticSparseAttention(nn.Module):
                            "in the reference's Triton kernel)", attention_dropout)
         self.pattern = PatternSpec(layer_idx, num_hidden_layers, attention_length)
         self._buffers_cache: dict = {}
+        # the backward's key plan for the current shapes (set .enabled = False
+        # to trade its memory, ~4 bytes per (query, head, slot), for the key
+        # side's pattern searches)
+        self.key_plans = KeyPlanCache()
 
     # -- pattern buffers (lazy; reference :446-468) --------------------------
     def _pattern_device(self) -> torch.device:
@@ -244,7 +277,7 @@ class ElasticSparseAttention(nn.Module):
         if needs_grad:
             res = ElasticSparseAttentionFunction.apply(
                 query_states, key_states, value_states, self.pattern, self.scaling,
-                self.num_kv_groups, rows, dropout_p, seed, want_weights)
+                self.num_kv_groups, rows, dropout_p, seed, want_weights, self.key_plans)
         else:
             # inference: no autograd node, nothing saved
             res = _forward_without_grad(query_states, key_states, value_states, self.pattern,

@@ -13,6 +13,7 @@
 #include <mutex>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -23,6 +24,7 @@
 #include "esa_keymma.cuh"
 #include "esa_layer.cuh"
 #include "esa_pattern.cuh"
+#include "esa_keyplan.cuh"
 #include "esa_probe.cuh"
 #include "esa_window_tc.cuh"
 #include "esa_window_bwd.cuh"
@@ -563,7 +565,10 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
       // workspace, the last writes dK / dV
       const int gs = p.acc ? KM::kHeadsPerLaunch : p.G;
       const size_t smem = KM::smem_bytes(gs * p.pat.w);
-      auto kern = esa::bwd_key_mma_kernel<T, D>;
+      // with a key plan (built for this problem with the same launch split)
+      // the tiles read their user records instead of searching the columns
+      const bool planned = p.plan_header && p.plan_nlaunch == (p.G + gs - 1) / gs;
+      auto kern = planned ? esa::bwd_key_mma_kernel<T, D, true> : esa::bwd_key_mma_kernel<T, D, false>;
       if (int rc = prepare_smem(kern, smem)) return rc;
       const int tile = KM::kWarps * KM::kTiles * KM::kKeys;
       dim3 grid((p.kv_rows + tile - 1) / tile, p.Hkv, p.B);
@@ -572,7 +577,7 @@ int launch_backward(const esa::AttnParams& p_in, cudaStream_t s) {
         pk.head_in_group = h0;
         pk.key_heads = std::min(gs, p.G - h0);
         {
-          LaunchTrace tr("bwd_key_mma", s);
+          LaunchTrace tr(planned ? "bwd_key_plan" : "bwd_key_mma", s);
           kern<<<grid, KM::kWarps * 32, smem, s>>>(pk);
         }
         if (int rc = check_launch("backward (key side, tensor cores)")) return rc;
@@ -670,11 +675,101 @@ size_t acc_bytes(const esa_problem_t* pb) {
                   sizeof(float));
 }
 
+// Key plan geometry (esa_keyplan.cuh) of a problem.
+struct PlanGeom {
+  int gs = 0, nlaunch = 0, ntiles = 0;
+  int64_t seg_users = 0, seg_heavy = 0;
+  size_t off_ustart = 0, off_hstart = 0, off_users = 0, off_heavy = 0, total = 0;
+};
+
+// Query heads per key-side launch when the backward of this problem runs the
+// tensor-core key side and a plan can describe it (as far as the problem
+// alone decides: tensor strides are checked at the call), else 0.
+struct PlanQuery {
+  template <typename T, int D>
+  static int run(const esa::AttnParams& p, cudaStream_t) {
+    if constexpr (std::is_same<T, float>::value || !(D == 64 || D == 128)) {
+      return 0;
+    } else {
+      using KM = esa::KeyMma<T, D>;
+      if (const int ht = window_heads_for_problem<T, D>(p)) {
+        const int nk = (esa::kWinRows / ht + p.pat.w - 1 + 15) / 16 * 16;
+        if (!(p.flags & ESA_FLAG_GATHER_ONLY) && nk <= esa::kWbqMaxKeys) return 0;
+      }
+      const int gs = p.G > 1 ? KM::kHeadsPerLaunch : 1;
+      const bool ok = !p.rows && p.G <= KM::kMaxGroup && p.G * p.pat.w <= KM::kMaxCols &&
+                      gs * p.pat.w <= esa::kPlanMaxCols && p.n_rows >= 1 &&
+                      p.n_rows <= (1 << esa::kPlanSlotBits) && p.kv_rows >= 1 &&
+                      !(p.flags & ESA_FLAG_GATHER_ONLY);
+      return ok ? gs : 0;
+    }
+  }
+};
+
+PlanGeom plan_geom(const esa_problem_t* pb, const esa::AttnParams& p) {
+  PlanGeom g;
+  g.gs = dispatch_op<PlanQuery>(pb->dtype, pb->head_dim, p, nullptr);
+  if (g.gs <= 0) {
+    g.gs = 0;
+    return g;
+  }
+  g.nlaunch = (p.G + g.gs - 1) / g.gs;
+  g.ntiles = (p.kv_rows + esa::kKeyPlanKeys - 1) / esa::kKeyPlanKeys;
+  const int64_t segs = (int64_t)p.Hkv * g.nlaunch;
+  g.seg_users = (int64_t)g.gs * p.pat.w * p.n_rows;
+  g.seg_heavy = (int64_t)g.gs * p.pat.w * (p.n_rows / esa::kHeavyChunk);
+  size_t off = align256(esa::kKeyPlanHeaderWords * sizeof(uint64_t));
+  g.off_ustart = off;
+  off += align256((size_t)segs * (g.ntiles + 1) * sizeof(int));
+  g.off_hstart = off;
+  off += align256((size_t)segs * (g.ntiles + 1) * sizeof(int));
+  g.off_users = off;
+  off += align256((size_t)segs * g.seg_users * sizeof(uint32_t));
+  g.off_heavy = off;
+  off += align256((size_t)segs * g.seg_heavy * sizeof(uint32_t));
+  g.total = off;
+  return g;
+}
+
+// FNV-1a over everything the plan depends on.
+uint64_t plan_fingerprint(const esa::AttnParams& p, const PlanGeom& g) {
+  uint64_t h = 0xcbf29ce484222325ull;
+  auto mix = [&](uint64_t v) {
+    for (int i = 0; i < 8; ++i) {
+      h ^= (v >> (8 * i)) & 0xff;
+      h *= 0x100000001b3ull;
+    }
+  };
+  uint32_t a, c;
+  std::memcpy(&a, &p.pat.a, 4);
+  std::memcpy(&c, &p.pat.c, 4);
+  const int64_t f[] = {p.pat.w, p.pat.num_heads, a, c, p.pat.head_offset, p.Hq, p.Hkv,
+                       p.n_rows, p.row_offset, p.kv_len, p.kv_offset, p.kv_rows,
+                       p.n_rows / esa::kHeavyChunk, g.gs, esa::kKeyPlanKeys};
+  for (int64_t v : f) mix((uint64_t)v);
+  return h;
+}
+
+void set_plan(esa::AttnParams& p, const void* plan, const PlanGeom& g) {
+  const unsigned char* b = static_cast<const unsigned char*>(plan);
+  p.plan_header = reinterpret_cast<const uint64_t*>(b);
+  p.plan_fp = plan_fingerprint(p, g);
+  p.plan_ustart = reinterpret_cast<const int*>(b + g.off_ustart);
+  p.plan_hstart = reinterpret_cast<const int*>(b + g.off_hstart);
+  p.plan_users = reinterpret_cast<const uint32_t*>(b + g.off_users);
+  p.plan_heavy = reinterpret_cast<const uint32_t*>(b + g.off_heavy);
+  p.plan_seg_users = g.seg_users;
+  p.plan_seg_heavy = g.seg_heavy;
+  p.plan_ntiles = g.ntiles;
+  p.plan_nlaunch = g.nlaunch;
+  p.plan_gs = g.gs;
+}
+
 }  // namespace
 
 extern "C" {
 
-int esa_version(void) { return 110; }
+int esa_version(void) { return 120; }
 
 const char* esa_last_error(void) { return g_last_error.c_str(); }
 
@@ -757,7 +852,51 @@ int esa_forward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_ten
   return dispatch_op<FwdOp>(pb->dtype, pb->head_dim, p, (cudaStream_t)stream);
 }
 
+size_t esa_key_plan_size(const esa_problem_t* pb) {
+  if (check_problem(pb) || pb->q_len == 0) return 0;
+  return plan_geom(pb, base_params(pb)).total;
+}
+
+int esa_key_plan_build(const esa_problem_t* pb, void* plan, size_t plan_bytes, void* stream) {
+  if (int rc = check_problem(pb)) return rc;
+  esa::AttnParams p = base_params(pb);
+  // the chunks the backward sums separately (bwd_heavy_kernel) are left out
+  // of the user lists, exactly as the backward's own key side leaves them
+  p.heavy_chunks = (int)(pb->q_len / esa::kHeavyChunk);
+  const PlanGeom g = pb->q_len > 0 ? plan_geom(pb, p) : PlanGeom{};
+  if (!g.total)
+    return fail(ESA_ERR_UNSUPPORTED, "esa_key_plan_build: this problem takes no key plan");
+  if (!plan || plan_bytes < g.total)
+    return fail(ESA_ERR_INVALID, "esa_key_plan_build: %zu bytes given, %zu needed", plan_bytes,
+                g.total);
+  if (reinterpret_cast<uintptr_t>(plan) % 256)
+    return fail(ESA_ERR_INVALID, "esa_key_plan_build: plan must be 256-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  unsigned char* b = static_cast<unsigned char*>(plan);
+  esa::KeyPlanBuild kb;
+  kb.gs = g.gs;
+  kb.nlaunch = g.nlaunch;
+  kb.ntiles = g.ntiles;
+  kb.seg_users = g.seg_users;
+  kb.seg_heavy = g.seg_heavy;
+  kb.ustart = reinterpret_cast<int*>(b + g.off_ustart);
+  kb.hstart = reinterpret_cast<int*>(b + g.off_hstart);
+  kb.users = reinterpret_cast<uint32_t*>(b + g.off_users);
+  kb.heavy = reinterpret_cast<uint32_t*>(b + g.off_heavy);
+  const int per_cta = esa::kKeyPlanWarps * esa::kKeyPlanTiles * esa::kKeyPlanKeys;
+  const dim3 grid((p.kv_rows + per_cta - 1) / per_cta, p.Hkv, g.nlaunch);
+  const size_t smem = (size_t)esa::kKeyPlanWarps * 2 * g.gs * p.pat.w * sizeof(int);
+  LaunchTrace tr("key_plan", s);
+  esa::key_plan_header_kernel<<<1, 32, 0, s>>>(reinterpret_cast<uint64_t*>(b),
+                                               plan_fingerprint(p, g));
+  esa::key_plan_kernel<false><<<grid, esa::kKeyPlanWarps * 32, smem, s>>>(p, kb);
+  esa::key_plan_scan_kernel<<<dim3((unsigned)(p.Hkv * g.nlaunch), 2), 1024, 0, s>>>(kb);
+  esa::key_plan_kernel<true><<<grid, esa::kKeyPlanWarps * 32, smem, s>>>(p, kb);
+  return check_launch("esa_key_plan_build");
+}
+
 size_t esa_backward_workspace_size(const esa_problem_t* pb) {
+
   if (!pb || pb->batch < 0 || pb->q_len < 0 || pb->attn_length < 0) return 0;
   return pds_bytes(pb) + acc_bytes(pb) + heavy_bytes(pb);
 }
@@ -790,6 +929,15 @@ int esa_backward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_te
   if (reinterpret_cast<uintptr_t>(workspace) % 256)
     return fail(ESA_ERR_INVALID, "workspace must be 256-byte aligned");
   esa::AttnParams p = base_params(pb);
+  if (pb->key_plan && pb->q_len > 0) {
+    const PlanGeom g = plan_geom(pb, p);
+    if (!g.total || pb->key_plan_bytes != g.total)
+      return fail(ESA_ERR_INVALID, "key_plan of %llu bytes given, this problem's plan has %zu",
+                  (unsigned long long)pb->key_plan_bytes, g.total);
+    if (reinterpret_cast<uintptr_t>(pb->key_plan) % 256)
+      return fail(ESA_ERR_INVALID, "key_plan must be 256-byte aligned");
+    set_plan(p, pb->key_plan, g);
+  }
   if (int rc = device_error_word(&p.err)) return rc;
   set_tensor(q, p.q, p.sqb, p.sqh, p.sqs);
   set_tensor(k, p.k, p.skb, p.skh, p.sks);
@@ -863,7 +1011,8 @@ struct ProbeOp {
       dim3 grid((p.n_rows + tq - 1) / tq, p.Hkv, p.B);
       auto kern = mode == esa::kProbePattern    ? esa::gather_probe_kernel<T, D, esa::kProbePattern>
                   : mode == esa::kProbeL2Random ? esa::gather_probe_kernel<T, D, esa::kProbeL2Random>
-                                                : esa::gather_probe_kernel<T, D, esa::kProbeL1Window>;
+                  : mode == esa::kProbeL1Window ? esa::gather_probe_kernel<T, D, esa::kProbeL1Window>
+                                                : esa::gather_probe_kernel<T, D, esa::kProbeL2Stream>;
       if (int rc = prepare_smem(kern, esa::kTileSmemBytes)) return rc;
       LaunchTrace tr("gather_probe", s);
       kern<<<grid, 256, esa::kTileSmemBytes, s>>>(p, sink);
@@ -877,7 +1026,7 @@ struct ProbeOp {
 extern "C" int esa_probe_gather(int32_t mode, const esa_problem_t* pb, esa_tensor_t k,
                                 esa_tensor_t v, uint32_t* sink, void* stream) {
   if (int rc = check_problem(pb)) return rc;
-  if (mode < ESA_PROBE_PATTERN || mode > ESA_PROBE_L1_WINDOW)
+  if (mode < ESA_PROBE_PATTERN || mode > ESA_PROBE_L2_STREAM)
     return fail(ESA_ERR_INVALID, "esa_probe_gather: unknown mode %d", mode);
   if (!sink) return fail(ESA_ERR_INVALID, "esa_probe_gather: null sink");
   if (pb->q_len == 0 || pb->batch == 0) return ESA_OK;

@@ -34,8 +34,11 @@
 // Per tile: (A) every column's user range and a flat prefix of the counts,
 // (B) all those users in one software pipeline, 32 per trip (user u ->
 // column by a binary search over a 32-column window of the prefix), (C) the
-// rare columns holding summed chunks.  Warp = kTiles consecutive tiles of 4
-// keys; CTA = kWarps warps.
+// rare columns holding summed chunks.  With a key plan (PLANNED, built once
+// per pattern by esa_keyplan.cuh) A-C are replaced by the tile's precomputed
+// user records and summed-chunk records: no searches and no index
+// arithmetic per user.  Warp = kTiles consecutive tiles of 4 keys; CTA =
+// kWarps warps.
 #pragma once
 #include "esa_common.cuh"
 #include "esa_params.h"
@@ -125,61 +128,29 @@ __device__ __forceinline__ void km_cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(KeyMma<T, D>::kWarps * 32, KeyMma<T, D>::kMinBlocks)
-bwd_key_mma_kernel(const AttnParams p) {
-  using C = KeyMma<T, D>;
-  constexpr int MT = D / 16;                      // 16-dim MMA row tiles
-  constexpr int UB = C::kUsers;
-  constexpr int NK = C::kKeys;
-  constexpr unsigned kAll = 0xffffffffu;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // this launch: query heads hh0 .. hh0 + GS - 1 of every group
-  const int w = p.pat.w, G = p.G, GS = p.key_heads, hh0 = p.head_in_group;
-  const int ncols = GS * w, nrounds = (ncols + 31) >> 5;
-  unsigned char* ring = smem_raw + warp * C::kRingBytes;
-  // per column: the cursor (first query slot whose key is >= the current
-  // tile's first key; after step A of a tile, >= the next tile's) and the
-  // exclusive prefix of the tile's streamed user counts
-  int* scur = reinterpret_cast<int*>(smem_raw + C::kWarps * C::kRingBytes) + warp * C::arrays(ncols);
-  int* soff = scur + ncols;
-  const int hkv = blockIdx.y, b = blockIdx.z;
-  const int lr0 = (blockIdx.x * C::kWarps + warp) * (C::kTiles * NK);
-  if (lr0 >= p.kv_rows) return;
-  const int n = p.n_rows;
-  const int kvmax = p.kv_len - 1;
-  // L2: the users' q / dO rows are re-read (a query row serves 64 keys spread
-  // over the sweep); the (p, dS) workspace passes once
-  const uint64_t pol_rows = l2_evict_last_policy();
-  const uint64_t pol_stream = l2_evict_first_policy();
-  // col -> (hh, k) with hh = col / w by a multiply-high (exact for col < 2^14, w <= 1024)
-  const unsigned long long wmagic = 0xffffffffull / (unsigned)w + 1ull;
-  // lane j (< GS) holds the head weight of query head hkv * G + hh0 + j
-  const float lane_t = head_weight(p.pat, hkv * G + hh0 + (lane < GS ? lane : 0));
-  auto cidx = [&](int jq, int k, float t) -> int {
+// Column geometry of the key side.  A column is one (query head, slot) pair;
+// its index is non-decreasing along query slots, so the users of a key range
+// are one query range, found by searching the column.
+struct KeyColumns {
+  const AttnParams& p;
+  int n, kvmax, w;
+  __device__ __forceinline__ explicit KeyColumns(const AttnParams& pp)
+      : p(pp), n(pp.n_rows), kvmax(pp.kv_len - 1), w(pp.pat.w) {}
+  // key of query slot jq in column (k, t) (clamped like the forward, :615)
+  __device__ __forceinline__ int cidx(int jq, int k, float t) const {
     return min(raw_index(row_window(p.pat, p.row_offset + jq), k, t, __fsub_rn(1.f, t)), kvmax);
-  };
-  // (hh, k, t, workspace column) of column col; every lane calls it (shuffle inside)
-  struct Col {
-    int hh, k, base;
-    float t;
-  };
-  auto column = [&](int col) {
-    Col c;
-    const int j = (int)(((unsigned long long)(unsigned)col * wmagic) >> 32);
-    c.hh = hh0 + j;
-    c.k = col - j * w;
-    c.t = __shfl_sync(kAll, lane_t, j & 31);
-    c.base = (b * p.Hq + hkv * G + c.hh) * w + c.k;
-    return c;
-  };
-
+  }
+  // Approximate keys per query slot along a column (the index grows by
+  // (1 - alpha) + (k + t) * alpha / w per position), for first guesses.
+  __device__ __forceinline__ float slope(int k, float t) const {
+    return fmaxf((1.f - p.pat.a) + (k + t) * p.pat.a / (float)w, 1e-6f);
+  }
   // First slot q in [lo0, n) of column (k, t) whose key is >= target, given
   // that slot lo0 - 1 (if any) is below it; starts at the guess g and
   // gallops from there (down if g is already at or above the target, up
   // otherwise), then bisects.  val = the key at the result (or INT_MAX at n).
-  auto find_first = [&](int lo0, int g, int target, int k, float t, int& val) {
+  __device__ __forceinline__ int find_first(int lo0, int g, int target, int k, float t,
+                                            int& val) const {
     int lo = lo0 - 1, hi = n, hv = 0x7fffffff;
     if (lo0 < n) {
       g = min(max(g, lo0), n - 1);
@@ -209,29 +180,93 @@ bwd_key_mma_kernel(const AttnParams p) {
     }
     val = hi < n ? hv : 0x7fffffff;
     return hi;
-  };
-  // Approximate keys per query slot along a column (the index grows by
-  // (1 - alpha) + (k + t) * alpha / w per position), for the first guesses.
-  auto slope = [&](int k, float t) {
-    return fmaxf((1.f - p.pat.a) + (k + t) * p.pat.a / (float)w, 1e-6f);
-  };
-
+  }
   // first query slot of column (k, t) whose key is >= P, searched from a guess:
   // the position whose key is about P, st + (k + t) * sp - t = P with
   // st = E (1 - alpha) - c and sp = (E alpha + c) / w, E = position + 1
-  auto first_user = [&](int P, int k, float t) {
+  __device__ __forceinline__ int first_user(int P, int k, float t) const {
     const float num = (float)P + p.pat.c + t - (k + t) * p.pat.c / (float)w;
     const float gq = num / slope(k, t) - 1.f - (float)p.row_offset;
     const int g = (int)fminf(fmaxf(gq, 0.f), (float)n);
     int v;
     return find_first(0, g, P, k, t, v);
+  }
+  // is chunk ch of column (k, t) one key throughout (summed by bwd_heavy_kernel)?
+  __device__ __forceinline__ bool constant_chunk(int ch, int k, float t) const {
+    return cidx(ch * kHeavyChunk, k, t) == cidx(ch * kHeavyChunk + kHeavyChunk - 1, k, t);
+  }
+};
+
+// Key plan records (esa_keyplan.cuh): user = column << 25 | (key - tile
+// start) << 23 | query slot; summed chunk = column << 25 | (key - tile
+// start) << 23 | chunk.  So a plan covers at most 2^23 query slots and 128
+// columns per launch.
+constexpr int kPlanSlotBits = 23;
+constexpr uint32_t kPlanSlotMask = (1u << kPlanSlotBits) - 1u;
+constexpr int kPlanColShift = 25;
+constexpr int kPlanMaxCols = 1 << (32 - kPlanColShift);
+
+template <typename T, int D, bool PLANNED>
+__global__ void __launch_bounds__(KeyMma<T, D>::kWarps * 32, KeyMma<T, D>::kMinBlocks)
+bwd_key_mma_kernel(const AttnParams p) {
+  using C = KeyMma<T, D>;
+  constexpr int MT = D / 16;                      // 16-dim MMA row tiles
+  constexpr int UB = C::kUsers;
+  constexpr int NK = C::kKeys;
+  constexpr unsigned kAll = 0xffffffffu;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // this launch: query heads hh0 .. hh0 + GS - 1 of every group
+  const int w = p.pat.w, G = p.G, GS = p.key_heads, hh0 = p.head_in_group;
+  const int ncols = GS * w, nrounds = (ncols + 31) >> 5;
+  unsigned char* ring = smem_raw + warp * C::kRingBytes;
+  // per column: the cursor (first query slot whose key is >= the current
+  // tile's first key; after step A of a tile, >= the next tile's) and the
+  // exclusive prefix of the tile's streamed user counts
+  int* scur = reinterpret_cast<int*>(smem_raw + C::kWarps * C::kRingBytes) + warp * C::arrays(ncols);
+  int* soff = scur + ncols;
+  const int hkv = blockIdx.y, b = blockIdx.z;
+  const int lr0 = (blockIdx.x * C::kWarps + warp) * (C::kTiles * NK);
+  if (lr0 >= p.kv_rows) return;
+  if constexpr (PLANNED) {
+    // a plan built for another problem: record it, write nothing
+    if (p.plan_header[1] != p.plan_fp) {
+      if (lane == 0 && p.err) atomicOr(p.err, kErrPlan);
+      return;
+    }
+  }
+  const int n = p.n_rows;
+  // L2: the users' q / dO rows are re-read (a query row serves 64 keys spread
+  // over the sweep); the (p, dS) workspace passes once
+  const uint64_t pol_rows = l2_evict_last_policy();
+  const uint64_t pol_stream = l2_evict_first_policy();
+  // col -> (hh, k) with hh = col / w by a multiply-high (exact for col < 2^14, w <= 1024)
+  const unsigned long long wmagic = 0xffffffffull / (unsigned)w + 1ull;
+  // lane j (< GS) holds the head weight of query head hkv * G + hh0 + j
+  const float lane_t = head_weight(p.pat, hkv * G + hh0 + (lane < GS ? lane : 0));
+  const KeyColumns kc(p);
+  // (hh, k, t, workspace column) of column col; every lane calls it (shuffle inside)
+  struct Col {
+    int hh, k, base;
+    float t;
+  };
+  auto column = [&](int col) {
+    Col c;
+    const int j = (int)(((unsigned long long)(unsigned)col * wmagic) >> 32);
+    c.hh = hh0 + j;
+    c.k = col - j * w;
+    c.t = __shfl_sync(kAll, lane_t, j & 31);
+    c.base = (b * p.Hq + hkv * G + c.hh) * w + c.k;
+    return c;
   };
 
   // Cursors: first query slot of each column whose key is >= the warp's first key.
-  for (int cc = 0; cc < nrounds; ++cc) {
-    const int col = cc * 32 + lane;
-    const Col c = column(col < ncols ? col : 0);
-    if (col < ncols) scur[col] = first_user(p.kv_offset + lr0, c.k, c.t);
+  if constexpr (!PLANNED) {
+    for (int cc = 0; cc < nrounds; ++cc) {
+      const int col = cc * 32 + lane;
+      const Col c = column(col < ncols ? col : 0);
+      if (col < ncols) scur[col] = kc.first_user(p.kv_offset + lr0, c.k, c.t);
+    }
   }
 
   const unsigned char* qbytes = reinterpret_cast<const unsigned char*>(
@@ -254,11 +289,6 @@ bwd_key_mma_kernel(const AttnParams p) {
   const uint32_t lm_user = (uint32_t)(lr + ((lj >> 1) << 3)) * C::kUserBytes;
   // B-fragment column g4 = part * 4 + key (part 0: hi terms, 1: lo terms)
   const int bkey = g4 & 3;
-  // is chunk ch of column (k, t) one key throughout (summed by bwd_heavy_kernel)?
-  auto constant_chunk = [&](int ch, int k, float t) {
-    return cidx(ch * kHeavyChunk, k, t) == cidx(ch * kHeavyChunk + kHeavyChunk - 1, k, t);
-  };
-
   float acck[MT][4], accv[MT][4];
 
   for (int tile = 0; tile < C::kTiles; ++tile) {
@@ -269,11 +299,28 @@ bwd_key_mma_kernel(const AttnParams p) {
     for (int i = 0; i < MT; ++i)
 #pragma unroll
       for (int e = 0; e < 4; ++e) { acck[i][e] = 0.f; accv[i][e] = 0.f; }
+    // adds the partial sums of summed chunk chk of workspace column sbase
+    // (heavy[(b * Hq + h) * w + k][chunk][{dK, dV}][D]) to key kk of the tile
+    auto add_partials = [&](int sbase, int chk, int kk) {
+      if (t4 != (kk >> 1)) return;
+      const float* part = p.heavy + ((int64_t)sbase * p.heavy_chunks + chk) * (2 * D);
+      const bool odd = kk & 1;
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        const float k0 = part[16 * i + g4], k1 = part[16 * i + g4 + 8];
+        const float v0 = part[D + 16 * i + g4], v1 = part[D + 16 * i + g4 + 8];
+        if (odd) {
+          acck[i][1] += k0; acck[i][3] += k1; accv[i][1] += v0; accv[i][3] += v1;
+        } else {
+          acck[i][0] += k0; acck[i][2] += k1; accv[i][0] += v0; accv[i][2] += v1;
+        }
+      }
+    };
 
-    // Streams `total` users through the MMAs.  resolve(t0, qi) -> Col of
-    // user t0 + lane (and its query slot qi); every lane calls it, once per
-    // trip of 32 users, t0 = 0, 32, 64, ...  The rows of a batch are in flight
-    // while the previous batch is multiplied.
+    // Streams `total` users through the MMAs.  resolve(t0, qi, key) -> Col of
+    // user t0 + lane (and its query slot qi; with a plan also its key - P0);
+    // every lane calls it, once per trip of 32 users, t0 = 0, 32, 64, ...  The
+    // rows of a batch are in flight while the previous batch is multiplied.
     auto stream = [&](const int total, auto&& resolve) {
       if (total <= 0) return;
       // One trip = 32 users (lane l: user t0 + l) = two batches of UB: users
@@ -284,11 +331,11 @@ bwd_key_mma_kernel(const AttnParams p) {
         int key;
         uint32_t oq, od;
       };
-      int qi_f;
+      int qi_f, key_f = 0;
       Col c_f;
       auto fetch = [&](int t0, U& r) {   // resolve, start the (p, dS) load
         const bool valid = t0 + lane < total;
-        c_f = resolve(t0, qi_f);
+        c_f = resolve(t0, qi_f, key_f);
         // past the end: slot 0 of column base 0 (in bounds), weights zeroed
         if (!valid) { qi_f = 0; c_f.hh = 0; c_f.base = 0; }
         const float2 pd = ldg_f2_hint(p.pds + (int64_t)c_f.base * n + qi_f, pol_stream);
@@ -297,7 +344,9 @@ bwd_key_mma_kernel(const AttnParams p) {
         r.od = (uint32_t)c_f.hh * dh16 + (uint32_t)qi_f * ds16;
       };
       auto key_of = [&](int t0) {
-        const int key = cidx(qi_f, c_f.k, c_f.t) - P0;
+        int key;
+        if constexpr (PLANNED) key = key_f;
+        else key = kc.cidx(qi_f, c_f.k, c_f.t) - P0;
         return t0 + lane < total ? key : 0;
       };
       // start the row copies of half h of trip t0 into stage st
@@ -378,171 +427,184 @@ bwd_key_mma_kernel(const AttnParams p) {
       __syncwarp();
     };
 
-    // ---- A: each column's users of [P0, P1): [scur_old, scur_new); flat
-    // prefix of the counts streamed in B.  A column whose range holds a chunk
-    // bwd_heavy_kernel summed streams nothing here (handled in C).
-    int run = 0;
-    bool any_heavy = false;
-    for (int cc = 0; cc < nrounds; ++cc) {
-      const int col = cc * 32 + lane;
-      const bool ok = col < ncols;
-      const Col c = column(ok ? col : 0);
-      int s = 0, e = 0;
-      bool heavy = false;
-      if (ok) {
-        s = scur[col];
-        e = s;
-        const int ev = s < n ? cidx(s, c.k, c.t) : 0x7fffffff;   // key at the cursor
-        if (ev < P1) {
-          // first slot after s whose key is >= P1, from the slope's guess
-          const float steps = (float)(P1 - ev) / slope(c.k, c.t);
-          const int g = s + (int)fminf(ceilf(steps), (float)n);
-          int v;
-          e = find_first(s + 1, g, P1, c.k, c.t, v);
-        }
-        scur[col] = e;
-        if (p.heavy_chunks > 0 && e - s >= kHeavyChunk) {
-          const int cend = min(e / kHeavyChunk, p.heavy_chunks);
-          for (int ch = (s + kHeavyChunk - 1) / kHeavyChunk; ch < cend && !heavy; ++ch)
-            heavy = constant_chunk(ch, c.k, c.t);
-        }
-      }
-      const int len = heavy ? 0 : e - s;
-      int off = len;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(kAll, off, o);
-        if (lane >= o) off += y;
-      }
-      if (ok) soff[col] = run + off - len;
-      run += __shfl_sync(kAll, off, 31);
-      any_heavy |= __any_sync(kAll, heavy);
-    }
-    __syncwarp();
-
-    // ---- B: the flat stream; user u -> the last column whose prefix is <= u.
-    // Per trip (users t0 .. t0 + 31) the lanes load the prefixes of the 32
-    // columns after an anchor column c0 (prefix <= t0) and each lane counts,
-    // by a binary search over the lanes, those at or before its user.
-    {
-      int c0 = 0;
-      // anchor c0: soff[c0] <= t0 at every trip
-      stream(run, [&](int t0, int& qi) {
+    if constexpr (PLANNED) {
+      // the tile's users and summed chunks from the plan
+      const int sg = hkv * p.plan_nlaunch + hh0 / p.plan_gs;
+      const int ti = lt / NK;
+      const int* us = p.plan_ustart + (int64_t)sg * (p.plan_ntiles + 1);
+      const uint32_t* ur = p.plan_users + (int64_t)sg * p.plan_seg_users;
+      // (every value read from the plan is clamped to its range, so even a
+      // damaged plan cannot make an access leave the buffers)
+      const int ub = min(max(us[ti], 0), (int)p.plan_seg_users);
+      const int nu = min(max(us[ti + 1], ub), (int)p.plan_seg_users) - ub;
+      stream(nu, [&](int t0, int& qi, int& key) {
         const int u = t0 + lane;
-        const int cl = c0 + 1 + lane;
-        const int bl = cl < ncols ? soff[cl] : 0x7fffffff;
-        int col, nxt;   // nxt: prefix of the column after col
-        if (__ballot_sync(kAll, bl <= t0 + 31) != kAll) {
-          int pos = 0;   // window columns starting at or before u (bl is non-decreasing)
-#pragma unroll
-          for (int sh = 16; sh >= 1; sh >>= 1) {
-            const int v = __shfl_sync(kAll, bl, pos + sh - 1);
-            if (v <= u) pos += sh;
-          }
-          col = c0 + pos;
-          nxt = min(__shfl_sync(kAll, bl, pos), run);   // soff[col + 1], run past the end
-          c0 += __popc(__ballot_sync(kAll, bl <= t0 + 32));
-        } else {
-          // more than 32 columns start inside the trip (empty columns): search
-          int lo = c0, hi = ncols;   // soff[lo] <= u < soff[hi] (hi = ncols: end)
-          while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (soff[mid] <= u) lo = mid; else hi = mid;
-          }
-          col = lo;
-          nxt = col + 1 < ncols ? soff[col + 1] : run;
-          c0 = __shfl_sync(kAll, col, 31);
-        }
-        // the column's users of this tile end at its cursor: [scur - len, scur)
-        qi = scur[col] - nxt + u;
-        return column(col);
+        const uint32_t rec = u < nu ? __ldg(ur + ub + u) : 0u;
+        qi = min((int)(rec & kPlanSlotMask), n - 1);
+        key = (int)((rec >> kPlanSlotBits) & 3u);
+        return column(min((int)(rec >> kPlanColShift), ncols - 1));
       });
-    }
-
-    // ---- C: columns with summed chunks: the pieces between those chunks, then
-    // the chunks' partial sums
-    if (any_heavy) {
+      const int* hs = p.plan_hstart + (int64_t)sg * (p.plan_ntiles + 1);
+      const uint32_t* hr = p.plan_heavy + (int64_t)sg * p.plan_seg_heavy;
+      const int hb = min(max(hs[ti], 0), (int)p.plan_seg_heavy);
+      const int he = min(max(hs[ti + 1], hb), (int)p.plan_seg_heavy);
+      for (int e = hb; e < he; ++e) {
+        const uint32_t rec = __ldg(hr + e);
+        const Col c = column(min((int)(rec >> kPlanColShift), ncols - 1));
+        add_partials(c.base, min((int)(rec & kPlanSlotMask), p.heavy_chunks - 1),
+                     (int)((rec >> kPlanSlotBits) & 3u));
+      }
+    } else {
+      // ---- A: each column's users of [P0, P1): [scur_old, scur_new); flat
+      // prefix of the counts streamed in B.  A column whose range holds a chunk
+      // bwd_heavy_kernel summed streams nothing here (handled in C).
+      int run = 0;
+      bool any_heavy = false;
       for (int cc = 0; cc < nrounds; ++cc) {
         const int col = cc * 32 + lane;
         const bool ok = col < ncols;
         const Col c = column(ok ? col : 0);
-        int cur = 0, e = 0;
+        int s = 0, e = 0;
+        bool heavy = false;
         if (ok) {
-          const int nxt = col + 1 < ncols ? soff[col + 1] : run;
-          e = scur[col];
-          if (nxt == soff[col] && e > 0)   // nothing streamed in B: empty or heavy
-            cur = first_user(P0, c.k, c.t);
-          else
-            cur = e;
-        }
-        while (__any_sync(kAll, cur < e)) {
-          int seg_e = e, hc0 = 0, hc1 = 0;
-          if (cur < e && p.heavy_chunks > 0 && e - cur >= kHeavyChunk) {
-            int ch = (cur + kHeavyChunk - 1) / kHeavyChunk;
+          s = scur[col];
+          e = s;
+          const int ev = s < n ? kc.cidx(s, c.k, c.t) : 0x7fffffff;   // key at the cursor
+          if (ev < P1) {
+            // first slot after s whose key is >= P1, from the slope's guess
+            const float steps = (float)(P1 - ev) / kc.slope(c.k, c.t);
+            const int g = s + (int)fminf(ceilf(steps), (float)n);
+            int v;
+            e = kc.find_first(s + 1, g, P1, c.k, c.t, v);
+          }
+          scur[col] = e;
+          if (p.heavy_chunks > 0 && e - s >= kHeavyChunk) {
             const int cend = min(e / kHeavyChunk, p.heavy_chunks);
-            while (ch < cend && !constant_chunk(ch, c.k, c.t)) ++ch;
-            if (ch < cend) {
-              int ch2 = ch + 1;
-              while (ch2 < cend && constant_chunk(ch2, c.k, c.t)) ++ch2;
-              seg_e = ch * kHeavyChunk;
-              hc0 = ch;
-              hc1 = ch2;
-            }
+            for (int ch = (s + kHeavyChunk - 1) / kHeavyChunk; ch < cend && !heavy; ++ch)
+              heavy = kc.constant_chunk(ch, c.k, c.t);
           }
-          const int len = cur < e ? seg_e - cur : 0;
-          int off = len;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(kAll, off, o);
-            if (lane >= o) off += y;
-          }
-          const int total = __shfl_sync(kAll, off, 31);
-          off -= len;
-          stream(total, [&](int t0, int& qi) {
-            const int u = t0 + lane;
-            int o = 0;
-#pragma unroll
+        }
+        const int len = heavy ? 0 : e - s;
+        int off = len;
+  #pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(kAll, off, o);
+          if (lane >= o) off += y;
+        }
+        if (ok) soff[col] = run + off - len;
+        run += __shfl_sync(kAll, off, 31);
+        any_heavy |= __any_sync(kAll, heavy);
+      }
+      __syncwarp();
+
+      // ---- B: the flat stream; user u -> the last column whose prefix is <= u.
+      // Per trip (users t0 .. t0 + 31) the lanes load the prefixes of the 32
+      // columns after an anchor column c0 (prefix <= t0) and each lane counts,
+      // by a binary search over the lanes, those at or before its user.
+      {
+        int c0 = 0;
+        // anchor c0: soff[c0] <= t0 at every trip
+        stream(run, [&](int t0, int& qi, int&) {
+          const int u = t0 + lane;
+          const int cl = c0 + 1 + lane;
+          const int bl = cl < ncols ? soff[cl] : 0x7fffffff;
+          int col, nxt;   // nxt: prefix of the column after col
+          if (__ballot_sync(kAll, bl <= t0 + 31) != kAll) {
+            int pos = 0;   // window columns starting at or before u (bl is non-decreasing)
+  #pragma unroll
             for (int sh = 16; sh >= 1; sh >>= 1) {
-              const int cand = o + sh;
-              if (__shfl_sync(kAll, off, cand) <= u) o = cand;
+              const int v = __shfl_sync(kAll, bl, pos + sh - 1);
+              if (v <= u) pos += sh;
             }
-            qi = __shfl_sync(kAll, cur, o) + (u - __shfl_sync(kAll, off, o));
-            const int oc = cc * 32 + o;
-            return column(oc < ncols ? oc : 0);
-          });
-          // partial sums of the skipped chunks, added to their key's hi column
-          unsigned hm = __ballot_sync(kAll, hc1 > hc0);
-          while (hm) {
-            const int src = __ffs(hm) - 1;
-            hm &= hm - 1;
-            const int a = __shfl_sync(kAll, hc0, src);
-            const int z = __shfl_sync(kAll, hc1, src);
-            const int sk = __shfl_sync(kAll, c.k, src);
-            const int sbase = __shfl_sync(kAll, c.base, src);
-            const float stt = __shfl_sync(kAll, c.t, src);
-            // partials: heavy[(b * Hq + h) * w + k][chunk][{dK, dV}][D]
-            const float* part0 = p.heavy + (int64_t)sbase * p.heavy_chunks * (2 * D);
-            for (int chk = a; chk < z; ++chk) {
-              const int kk = cidx(chk * kHeavyChunk, sk, stt) - P0;   // same on every lane
-              if (t4 == (kk >> 1)) {
-                const float* part = part0 + (int64_t)chk * (2 * D);
-                const bool odd = kk & 1;
-#pragma unroll
-                for (int i = 0; i < MT; ++i) {
-                  const float k0 = part[16 * i + g4], k1 = part[16 * i + g4 + 8];
-                  const float v0 = part[D + 16 * i + g4], v1 = part[D + 16 * i + g4 + 8];
-                  if (odd) {
-                    acck[i][1] += k0; acck[i][3] += k1; accv[i][1] += v0; accv[i][3] += v1;
-                  } else {
-                    acck[i][0] += k0; acck[i][2] += k1; accv[i][0] += v0; accv[i][2] += v1;
-                  }
-                }
+            col = c0 + pos;
+            nxt = min(__shfl_sync(kAll, bl, pos), run);   // soff[col + 1], run past the end
+            c0 += __popc(__ballot_sync(kAll, bl <= t0 + 32));
+          } else {
+            // more than 32 columns start inside the trip (empty columns): search
+            int lo = c0, hi = ncols;   // soff[lo] <= u < soff[hi] (hi = ncols: end)
+            while (hi - lo > 1) {
+              const int mid = (lo + hi) >> 1;
+              if (soff[mid] <= u) lo = mid; else hi = mid;
+            }
+            col = lo;
+            nxt = col + 1 < ncols ? soff[col + 1] : run;
+            c0 = __shfl_sync(kAll, col, 31);
+          }
+          // the column's users of this tile end at its cursor: [scur - len, scur)
+          qi = scur[col] - nxt + u;
+          return column(col);
+        });
+      }
+
+      // ---- C: columns with summed chunks: the pieces between those chunks, then
+      // the chunks' partial sums
+      if (any_heavy) {
+        for (int cc = 0; cc < nrounds; ++cc) {
+          const int col = cc * 32 + lane;
+          const bool ok = col < ncols;
+          const Col c = column(ok ? col : 0);
+          int cur = 0, e = 0;
+          if (ok) {
+            const int nxt = col + 1 < ncols ? soff[col + 1] : run;
+            e = scur[col];
+            if (nxt == soff[col] && e > 0)   // nothing streamed in B: empty or heavy
+              cur = kc.first_user(P0, c.k, c.t);
+            else
+              cur = e;
+          }
+          while (__any_sync(kAll, cur < e)) {
+            int seg_e = e, hc0 = 0, hc1 = 0;
+            if (cur < e && p.heavy_chunks > 0 && e - cur >= kHeavyChunk) {
+              int ch = (cur + kHeavyChunk - 1) / kHeavyChunk;
+              const int cend = min(e / kHeavyChunk, p.heavy_chunks);
+              while (ch < cend && !kc.constant_chunk(ch, c.k, c.t)) ++ch;
+              if (ch < cend) {
+                int ch2 = ch + 1;
+                while (ch2 < cend && kc.constant_chunk(ch2, c.k, c.t)) ++ch2;
+                seg_e = ch * kHeavyChunk;
+                hc0 = ch;
+                hc1 = ch2;
               }
             }
+            const int len = cur < e ? seg_e - cur : 0;
+            int off = len;
+  #pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const int y = __shfl_up_sync(kAll, off, o);
+              if (lane >= o) off += y;
+            }
+            const int total = __shfl_sync(kAll, off, 31);
+            off -= len;
+            stream(total, [&](int t0, int& qi, int&) {
+              const int u = t0 + lane;
+              int o = 0;
+  #pragma unroll
+              for (int sh = 16; sh >= 1; sh >>= 1) {
+                const int cand = o + sh;
+                if (__shfl_sync(kAll, off, cand) <= u) o = cand;
+              }
+              qi = __shfl_sync(kAll, cur, o) + (u - __shfl_sync(kAll, off, o));
+              const int oc = cc * 32 + o;
+              return column(oc < ncols ? oc : 0);
+            });
+            // partial sums of the skipped chunks, added to their key's hi column
+            unsigned hm = __ballot_sync(kAll, hc1 > hc0);
+            while (hm) {
+              const int src = __ffs(hm) - 1;
+              hm &= hm - 1;
+              const int a = __shfl_sync(kAll, hc0, src);
+              const int z = __shfl_sync(kAll, hc1, src);
+              const int sk = __shfl_sync(kAll, c.k, src);
+              const int sbase = __shfl_sync(kAll, c.base, src);
+              const float stt = __shfl_sync(kAll, c.t, src);
+              for (int chk = a; chk < z; ++chk)   // the key is the same on every lane
+                add_partials(sbase, chk, kc.cidx(chk * kHeavyChunk, sk, stt) - P0);
+            }
+            cur = hc1 > hc0 ? hc1 * kHeavyChunk : e;
           }
-          cur = hc1 > hc0 ? hc1 * kHeavyChunk : e;
         }
       }
+
     }
 
     // ---- epilogue: hi + lo columns (lanes t4 and t4 ^ 2) -> fp32 [2][4 keys][D]

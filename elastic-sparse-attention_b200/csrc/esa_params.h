@@ -52,6 +52,21 @@ struct AttnParams {
   // fp32 [B, Hq, w, heavy_chunks, 2, D]; heavy_chunks = n_rows / kHeavyChunk.
   float* heavy;
   int heavy_chunks;
+  // Key plan (optional): the tensor-core key side's user lists, precomputed
+  // from the pattern (esa_keyplan.cuh).  Segment sg = hkv * plan_nlaunch +
+  // launch holds, per tile of 4 keys, its users as packed records
+  // (column << 25 | key - tile start << 23 | query slot) in
+  // [plan_ustart[sg][tile], plan_ustart[sg][tile + 1]) of plan_users + sg *
+  // plan_seg_users, and its summed long-run chunks (column << 25 | key << 23 |
+  // chunk) likewise in plan_hstart / plan_heavy.
+  const uint64_t* plan_header;  // nullptr = no plan
+  uint64_t plan_fp;             // fingerprint of the problem the plan must match
+  const int* plan_ustart;
+  const int* plan_hstart;
+  const uint32_t* plan_users;
+  const uint32_t* plan_heavy;
+  int64_t plan_seg_users, plan_seg_heavy;
+  int plan_ntiles, plan_nlaunch, plan_gs;   // plan_gs: query heads per launch
 };
 
 constexpr int kHeavyChunk = 1024;
@@ -69,6 +84,7 @@ __device__ __forceinline__ bool dropout_keep(const AttnParams& p, int pos, int b
 enum ErrBits : int {
   kErrKvRange = 1,     // an index fell outside the k/v rows handed to the launch
   kErrQueryRange = 4,  // a rows[] entry outside [-kv_len, kv_len)
+  kErrPlan = 8,        // the key plan was built for another problem
 };
 
 }  // namespace esa

@@ -11,14 +11,15 @@
 // pattern (the
 // tile kernels' exact stream), uniformly at random over the KV head's rows
 // (an L2-resident random gather), or at random within 64 rows per CTA (an
-// L1-resident gather).  The loaded words are folded into an xor checksum
+// L1-resident gather), or as runs of consecutive rows that no CTA reads
+// twice (L2 streaming).  The loaded words are folded into an xor checksum
 // that is stored only when it equals an improbable constant.
 #pragma once
 #include "esa_gather.cuh"
 
 namespace esa {
 
-enum ProbeMode : int { kProbePattern = 0, kProbeL2Random = 1, kProbeL1Window = 2 };
+enum ProbeMode : int { kProbePattern = 0, kProbeL2Random = 1, kProbeL1Window = 2, kProbeL2Stream = 3 };
 constexpr int kProbeWindowRows = 64;
 
 // 32-bit integer mix (xor-shift / multiply rounds) for the random row choices.
@@ -67,9 +68,16 @@ gather_probe_kernel(const AttnParams p, uint32_t* sink) {
       int v[2];
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        const uint32_t hsh = probe_mix(cta * 8192u + (uint32_t)(pi * kTileMaxW + k0 + i));
-        v[i] = MODE == kProbeL2Random ? (int)(hsh % (uint32_t)p.kv_rows)
-                                      : win0 + (int)(hsh & (kProbeWindowRows - 1));
+        if constexpr (MODE == kProbeL2Stream) {
+          // CTA c, pair pi, slot k: row (c * 128 * 64 + pi * 64 + k) mod kv_rows
+          const uint32_t r = (cta * (uint32_t)kTilePairs + (uint32_t)pi) * (uint32_t)kTileMaxW +
+                             (uint32_t)(k0 + i);
+          v[i] = (int)(r % (uint32_t)p.kv_rows);
+        } else {
+          const uint32_t hsh = probe_mix(cta * 8192u + (uint32_t)(pi * kTileMaxW + k0 + i));
+          v[i] = MODE == kProbeL2Random ? (int)(hsh % (uint32_t)p.kv_rows)
+                                        : win0 + (int)(hsh & (kProbeWindowRows - 1));
+        }
       }
       return make_int2(v[0], v[1]);
     }

@@ -37,7 +37,7 @@ import torch.nn.functional as F
 import torch.utils.checkpoint
 
 from . import layer_ops, ops
-from .attention import _ensure_monotone
+from .attention import KeyPlanCache, _ensure_monotone
 from .ops import PatternSpec
 
 
@@ -78,7 +78,8 @@ class _AttentionBlock(torch.autograd.Function):
     """a = attention(rope(y Wqkv^T)) Wo^T with the layouts described above."""
 
     @staticmethod
-    def forward(ctx, y, wqkv, wo, spec: PatternSpec, heads: tuple, inv_freq, positions):
+    def forward(ctx, y, wqkv, wo, spec: PatternSpec, heads: tuple, inv_freq, positions,
+                plans=None):
         Hq, Hkv, D = heads
         B, L, d = y.shape
         qkv = torch.matmul(y, wqkv.t())                       # [B, L, (Hq + 2 Hkv) D]
@@ -91,6 +92,7 @@ class _AttentionBlock(torch.autograd.Function):
         a = torch.matmul(o_rows, wo.t())
         ctx.save_for_backward(y, wqkv, wo, qkv, o_rows, lse, inv_freq, positions, probs)
         ctx.meta = (spec, heads, scale)
+        ctx.plans = plans
         return a
 
     @staticmethod
@@ -106,13 +108,14 @@ class _AttentionBlock(torch.autograd.Function):
         dqkv = torch.empty_like(qkv)
         dq, dk, dv = _split_heads(dqkv, B, L, Hq, Hkv, D)
         _ensure_monotone(Hq, spec, max(L, 2), y.device)
+        plan = ctx.plans.get(q, k, spec) if ctx.plans is not None else None
         ops.backward(q, k, v, o, lse, do_rows.view(B, L, Hq, D).transpose(1, 2), spec, scale,
-                     dq=dq, dk=dk, dv=dv, probs=probs)
+                     dq=dq, dk=dk, dv=dv, probs=probs, key_plan=plan)
         del do_rows
         layer_ops.rope_(dq, dk, inv_freq, positions, inverse=True)
         dy = torch.matmul(dqkv, wqkv)
         dwqkv = torch.matmul(dqkv.reshape(-1, dqkv.shape[-1]).t(), y.reshape(-1, d))
-        return dy, dwqkv, dwo, None, None, None, None
+        return dy, dwqkv, dwo, None, None, None, None, None
 
 
 def _split_heads(qkv, B, L, Hq, Hkv, D):
@@ -234,6 +237,8 @@ class ElasticDecoderStack(nn.Module):
         self.loss_chunk_rows = loss_chunk_rows
         self.specs = [PatternSpec(i, num_hidden_layers, attention_length)
                       for i in range(num_hidden_layers)]
+        # per layer: the backward's key plan for the current shapes
+        self.key_plans = [KeyPlanCache() for _ in range(num_hidden_layers)]
         kw = dict(dtype=dtype, device=device)
         self.embed = nn.Parameter(torch.empty(vocab_size, hidden_size, **kw))
         self.layers = nn.ModuleList(
@@ -252,7 +257,8 @@ class ElasticDecoderStack(nn.Module):
     def _layer(self, i: int, h, y, positions):
         lw = self.layers[i]
         a = _AttentionBlock.apply(y, lw.qkv_proj, lw.o_proj, self.specs[i],
-                                  (self.Hq, self.Hkv, self.D), self.inv_freq, positions)
+                                  (self.Hq, self.Hkv, self.D), self.inv_freq, positions,
+                                  self.key_plans[i])
         h, y2 = _AddRMSNorm.apply(h, a, lw.post_attention_norm, self.eps)
         m = _MLPBlock.apply(y2, lw.gate_up_proj, lw.down_proj)
         next_w = self.layers[i + 1].input_norm if i + 1 < len(self.layers) else self.final_norm

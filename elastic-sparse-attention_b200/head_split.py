@@ -18,7 +18,7 @@ from typing import Optional
 import torch
 import torch.nn as nn
 
-from .attention import ElasticSparseAttentionFunction, _forward_without_grad
+from .attention import ElasticSparseAttentionFunction, KeyPlanCache, _forward_without_grad
 from .ops import PatternSpec, MAX_POSITION
 
 
@@ -72,6 +72,7 @@ class HeadShardedElasticSparseAttention(nn.Module):
         self.num_kv_groups = num_attention_heads // self.num_key_value_heads
         self.pattern = PatternSpec(layer_idx, num_hidden_layers, attention_length).heads(
             num_attention_heads, self.head0)
+        self.key_plans = KeyPlanCache()
 
     def forward(self, query_states: torch.Tensor, key_states: torch.Tensor,
                 value_states: torch.Tensor) -> torch.Tensor:
@@ -89,7 +90,8 @@ class HeadShardedElasticSparseAttention(nn.Module):
         if needs_grad:
             out = ElasticSparseAttentionFunction.apply(query_states, key_states, value_states,
                                                        self.pattern, self.scaling,
-                                                       self.num_kv_groups)
+                                                       self.num_kv_groups, None, 0.0, 0, False,
+                                                       self.key_plans)
         else:
             out = _forward_without_grad(query_states, key_states, value_states, self.pattern,
                                         self.scaling, self.num_kv_groups, None, 0.0, 0, False)

@@ -110,7 +110,7 @@ def device_errors(device=None, clear: bool = True) -> int:
 
 def _problem(q, k, spec: PatternSpec, scale: float, rows, row_offset: int, kv_len: int,
              kv_offset: int, flags: int = 0, dropout_p: float = 0.0, dropout_seed: int = 0,
-             weights=None, probs=None):
+             weights=None, probs=None, key_plan=None):
     B, Hq, Lq, D = q.shape
     return _lib.problem(dtype=q.dtype, batch=B, num_heads=Hq, num_kv_heads=k.shape[1], head_dim=D,
                         attn_length=spec.attention_length, layer_idx=spec.layer_idx,
@@ -118,7 +118,28 @@ def _problem(q, k, spec: PatternSpec, scale: float, rows, row_offset: int, kv_le
                         kv_offset=kv_offset, kv_rows=k.shape[2], row_offset=row_offset,
                         rows=rows, scale=scale, flags=flags, dropout_p=dropout_p,
                         dropout_seed=dropout_seed, weights=weights, probs=probs,
-                        head_offset=spec.head_offset, pattern_heads=spec.pattern_heads)
+                        head_offset=spec.head_offset, pattern_heads=spec.pattern_heads,
+                        key_plan=key_plan)
+
+
+def key_plan(q, k, spec: PatternSpec, row_offset: int = 0, kv_len: int | None = None,
+             kv_offset: int = 0) -> torch.Tensor | None:
+    """The backward key side's precomputed user lists for this layer and these
+    shapes / offsets (a uint8 device buffer), or None when its backward takes
+    no plan.  Independent of the batch size and of the data: build it once and
+    pass it to every :func:`backward` of the layer with the same shapes."""
+    dev = _check_device(q, k)
+    pb = _problem(q, k, spec, 1.0, None, row_offset, k.shape[2] if kv_len is None else kv_len,
+                  kv_offset)
+    lib = _lib.load()
+    need = int(lib.esa_key_plan_size(ctypes.byref(pb)))
+    if need == 0:
+        return None
+    plan = torch.empty(need, dtype=torch.uint8, device=dev)
+    with _on(dev):
+        _lib.check(lib.esa_key_plan_build(ctypes.byref(pb), plan.data_ptr(), need,
+                                          _lib.stream_handle(dev)), "esa_key_plan_build")
+    return plan
 
 
 def probs_buffer(q, k, spec: PatternSpec, rows: torch.Tensor | None = None, row_offset: int = 0,
@@ -172,12 +193,15 @@ def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
              rows: torch.Tensor | None = None, row_offset: int = 0, kv_len: int | None = None,
              kv_offset: int = 0, sorted_rows=None, row_perm=None, workspace=None,
              dropout_p: float = 0.0, dropout_seed: int = 0, dq=None, dk=None, dv=None,
-             probs: torch.Tensor | None = None, gather_only: bool = False):
+             probs: torch.Tensor | None = None, gather_only: bool = False,
+             key_plan: torch.Tensor | None = None):
     """Backward pass.  Returns (dq, dk, dv) in the input dtype.  With dropout,
     pass the forward's dropout_p and dropout_seed (the keep mask is rebuilt).
     dq / dk / dv may be given as (strided) views to write the gradients into,
     e.g. the q / k / v parts of one fused QKV gradient buffer.  ``gather_only``
-    keeps sliding-window layers off the tensor-core backward (cross-checks)."""
+    keeps sliding-window layers off the tensor-core backward (cross-checks).
+    ``key_plan`` (from :func:`key_plan` for the same problem) spares the key
+    side its pattern searches."""
     dev = _check_device(q, k, v, o, lse, dout)
     dq = torch.empty_like(q) if dq is None else dq
     dk = torch.empty_like(k) if dk is None else dk
@@ -187,9 +211,12 @@ def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
             raise ValueError("gradient buffers must match the shapes and dtypes of q, k, v")
     if probs is not None:
         _check_probs(probs, q, spec)
+    if key_plan is not None and (key_plan.dtype != torch.uint8 or key_plan.device != dev
+                                 or not key_plan.is_contiguous()):
+        raise ValueError("key_plan must be the contiguous uint8 buffer from key_plan()")
     pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
                   kv_offset, _lib.FLAG_GATHER_ONLY if gather_only else 0, dropout_p,
-                  dropout_seed, None, probs)
+                  dropout_seed, None, probs, key_plan)
     lib = _lib.load()
     need = lib.esa_backward_workspace_size(ctypes.byref(pb))
     if workspace is None or workspace.numel() < need:

@@ -93,6 +93,14 @@ typedef struct {
  *                         holds every head.  This lets a caller split one
  *                         layer's heads over GPUs or launches; num_kv_heads
  *                         are then the K/V heads of those query heads.
+ *   key_plan,          -- optional device buffer filled by esa_key_plan_build
+ *   key_plan_bytes        for this problem (same pattern, shapes and offsets;
+ *                         key_plan_bytes = esa_key_plan_size(problem)): the
+ *                         backward's key side then reads its precomputed user
+ *                         lists instead of searching the pattern.  NULL / 0 =
+ *                         no plan.  A plan built for another problem is
+ *                         rejected (ESA_ERR_INVALID when its size differs,
+ *                         else ESA_DEVERR_PLAN and dk / dv left unwritten).
  */
 typedef struct {
   int32_t dtype;
@@ -118,6 +126,8 @@ typedef struct {
   void* probs;
   int32_t pattern_heads;
   int32_t reserved;   /* 0 */
+  const void* key_plan;
+  uint64_t key_plan_bytes;
 } esa_problem_t;
 
 /* flags: run every layer on the CUDA-core gather kernels, also where the
@@ -132,9 +142,12 @@ typedef struct {
                                      up; its tile was not written */
 #define ESA_DEVERR_QUERY_RANGE 4  /* a rows[] entry outside [-kv_len, kv_len);
                                      its output row is zero */
+#define ESA_DEVERR_PLAN 8         /* esa_backward was given a key plan built for
+                                     another problem; dk / dv not written */
 
-/* Library version, e.g. 110 for 0.1.1 (110 added head_offset / pattern_heads
- * to esa_problem_t, the launch trace and the gather probe). */
+/* Library version, e.g. 120 for 0.1.2 (110 added head_offset / pattern_heads
+ * to esa_problem_t, the launch trace and the gather probe; 120 the key plan:
+ * key_plan / key_plan_bytes in esa_problem_t, esa_key_plan_size / _build). */
 int esa_version(void);
 
 /* Message of the last failing call on this thread ("" if none). */
@@ -196,6 +209,23 @@ int esa_forward(const esa_problem_t* prob, esa_tensor_t q, esa_tensor_t k, esa_t
 size_t esa_backward_workspace_size(const esa_problem_t* prob);
 
 /*
+ * Key plan (no reference counterpart: the reference keeps its index buffers
+ * [H, max_seq_len, w] from construction, :454-468; this is the transposed,
+ * key-ordered form the backward's key side needs).  It depends only on the
+ * pattern, shapes and offsets of the problem (not on batch size or data), so
+ * a caller builds it once and passes it (problem.key_plan) to every backward
+ * of that layer.
+ *   esa_key_plan_size   bytes of the plan; 0 when this problem's key side
+ *                       takes no plan (sliding-window layers, fp32, head_dim
+ *                       other than 64 / 128, explicit rows, more than 2^23
+ *                       query rows)
+ *   esa_key_plan_build  fills a device buffer of that size (256-byte aligned)
+ *                       on `stream`
+ */
+size_t esa_key_plan_size(const esa_problem_t* prob);
+int esa_key_plan_build(const esa_problem_t* prob, void* plan, size_t plan_bytes, void* stream);
+
+/*
  * Backward.  Takes the forward's o and lse and the upstream gradient dout
  * (all [B, Hq, q_len, D]); writes dq [B, Hq, q_len, D] and dk/dv
  * [B, Hkv, kv_rows, D], fully (no zero-initialisation needed, no atomics).
@@ -238,11 +268,16 @@ int esa_trace_read(int32_t i, const char** name, float* ms);
  *                        KV head's kv_rows (one KV head at a time: L2-resident)
  *   ESA_PROBE_L1_WINDOW  the same number of rows, random within 64 rows per
  *                        CTA (K and V: 32 KB at D = 128, L1-resident)
+ *   ESA_PROBE_L2_STREAM  the same number of rows, each pair's slots reading
+ *                        consecutive rows and no row read twice by a CTA
+ *                        (runs of rows from L2 with no L1 reuse, the access
+ *                        pattern of the key side's user rows)
  * The elapsed time gives the achievable row-gather bandwidth of each level.
  */
 #define ESA_PROBE_PATTERN 0
 #define ESA_PROBE_L2_RANDOM 1
 #define ESA_PROBE_L1_WINDOW 2
+#define ESA_PROBE_L2_STREAM 3
 int esa_probe_gather(int32_t mode, const esa_problem_t* prob, esa_tensor_t k, esa_tensor_t v,
                      uint32_t* sink, void* stream);
 

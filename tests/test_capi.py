@@ -46,6 +46,8 @@ def test_struct_layout_matches_header(tmp_path, esa):
         ' printf(" %zu %zu %zu %zu %zu\\n", offsetof(esa_problem_t, dropout_seed),'
         " offsetof(esa_problem_t, weights), offsetof(esa_problem_t, probs),"
         " offsetof(esa_problem_t, head_offset), offsetof(esa_problem_t, pattern_heads));\n"
+        ' printf(" %zu %zu\\n", offsetof(esa_problem_t, key_plan),'
+        " offsetof(esa_problem_t, key_plan_bytes));\n"
         " return 0; }\n")
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-std=c99", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)],
@@ -55,7 +57,8 @@ def test_struct_layout_matches_header(tmp_path, esa):
     P, T = esa._lib.EsaProblem, esa._lib.EsaTensor
     want = [ctypes.sizeof(P), P.q_len.offset, P.rows.offset, P.scale.offset, ctypes.sizeof(T),
             T.stride_s.offset, P.row_offset.offset, P.dropout_seed.offset, P.weights.offset,
-            P.probs.offset, P.head_offset.offset, P.pattern_heads.offset]
+            P.probs.offset, P.head_offset.offset, P.pattern_heads.offset, P.key_plan.offset,
+            P.key_plan_bytes.offset]
     assert got == want
 
 
@@ -64,9 +67,53 @@ def _problem(esa, **kw):
                 num_kv_heads=2, head_dim=128, attn_length=64, layer_idx=3, num_hidden_layers=8,
                 q_len=16, kv_len=16, kv_offset=0, kv_rows=16, row_offset=0, rows=None,
                 scale=128 ** -0.5, flags=0, dropout_p=0.0, head_offset=0, dropout_seed=0,
-                weights=None, probs=None, pattern_heads=0, reserved=0)
+                weights=None, probs=None, pattern_heads=0, reserved=0, key_plan=None,
+                key_plan_bytes=0)
     base.update(kw)
     return esa._lib.EsaProblem(**base)
+
+
+def _plan_bytes(segs, ntiles, seg_users, seg_heavy):
+    a = lambda x: (x + 255) // 256 * 256
+    return a(32 * 8) + 2 * a(segs * (ntiles + 1) * 4) + a(segs * seg_users * 4) + \
+        a(segs * seg_heavy * 4)
+
+
+def test_key_plan_size(esa):
+    """The key plan's size (host-side: no device work) and where it applies:
+    one segment per (KV head, launch of 2 query heads of a group), a tile per
+    4 keys, at most one record per (query, head, slot)."""
+    lib = esa._lib.load()
+    size = lambda **kw: lib.esa_key_plan_size(ctypes.byref(_problem(esa, **kw)))
+    L = 4096
+    # G = 2: one launch per KV head
+    assert size(q_len=L, kv_len=L, kv_rows=L) == _plan_bytes(2, L // 4, 2 * 64 * L, 2 * 64 * 4)
+    # G = 4 (8 query / 2 KV heads): two launches of 2 heads per KV head
+    assert size(num_heads=8, q_len=L, kv_len=L, kv_rows=L) == \
+        _plan_bytes(4, L // 4, 2 * 64 * L, 2 * 64 * 4)
+    # MHA: one head per launch
+    assert size(num_kv_heads=4, q_len=L, kv_len=L, kv_rows=L) == \
+        _plan_bytes(4, L // 4, 64 * L, 64 * 4)
+    # no plan: the tensor-core window backward (layer 0, G = 4), fp32, other
+    # head_dim, explicit rows, the gather-only flag, an empty call
+    assert size(num_heads=8, layer_idx=0, q_len=L, kv_len=L, kv_rows=L) == 0
+    assert size(dtype=esa._lib.DTYPES[__import__("torch").float32], q_len=L, kv_len=L,
+                kv_rows=L) == 0
+    assert size(head_dim=32, q_len=L, kv_len=L, kv_rows=L) == 0
+    assert size(rows=1 << 20, q_len=L, kv_len=L, kv_rows=L) == 0
+    assert size(flags=1, q_len=L, kv_len=L, kv_rows=L) == 0
+    assert size(q_len=0) == 0
+
+
+def test_backward_rejects_mismatched_key_plan(esa):
+    lib = esa._lib.load()
+    L = 4096
+    pb = _problem(esa, q_len=L, kv_len=L, kv_rows=L, key_plan=1 << 20, key_plan_bytes=12345)
+    t = esa._lib.EsaTensor(1 << 20, 4096, 1024, 128)
+    ws = lib.esa_backward_workspace_size(ctypes.byref(pb))
+    rc = lib.esa_backward(ctypes.byref(pb), t, t, t, t, 1 << 20, t, t, t, t, None, None,
+                          1 << 20, ws, None)
+    assert rc == -1 and "key_plan" in lib.esa_last_error().decode()
 
 
 @pytest.mark.parametrize("kw,code,frag", [

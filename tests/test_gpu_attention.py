@@ -648,3 +648,26 @@ def test_head_sharded_module_matches_full_module(esa):
         assert torch.equal(qq.grad, full[1][:, h0:h0 + nh])
         assert torch.equal(kk.grad, full[2][:, kv0:kv0 + nkv])
         assert torch.equal(vv.grad, full[3][:, kv0:kv0 + nkv])
+
+
+def test_gather_probe_modes(esa):
+    """The gather probe (measurement aid) runs in every mode on a tile-kernel
+    problem, records no device error, and refuses an unknown mode."""
+    import ctypes
+    g = torch.Generator().manual_seed(3)
+    dt = torch.bfloat16
+    q = randn(1, 8, 2048, 128, dtype=dt, gen=g)
+    k, v = randn(1, 2, 2048, 128, dtype=dt, gen=g), randn(1, 2, 2048, 128, dtype=dt, gen=g)
+    lib = esa._lib.load()
+    pb = esa.ops._problem(q, k, esa.PatternSpec(5, 8, 64), 128 ** -0.5, None, 0, 2048, 0)
+    sink = torch.zeros(4, dtype=torch.int32, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    esa.ops.device_errors()
+    for mode in range(4):
+        rc = lib.esa_probe_gather(mode, ctypes.byref(pb), esa._lib.tensor4(k), esa._lib.tensor4(v),
+                                  sink.data_ptr(), stream)
+        assert rc == 0, lib.esa_last_error()
+    torch.cuda.synchronize()
+    assert esa.ops.device_errors() == 0
+    assert lib.esa_probe_gather(4, ctypes.byref(pb), esa._lib.tensor4(k), esa._lib.tensor4(v),
+                                sink.data_ptr(), stream) == -1

@@ -1,5 +1,5 @@
-"""GPU, 2 processes x 1 GPU each (NCCL): the sequence-sharded module against
-the fp32 oracle, outputs and all gradients.  Skipped when fewer than two GPUs
+"""GPU, 2 or 4 processes x 1 GPU each (NCCL): the sequence-sharded module
+against the fp32 oracle, outputs and all gradients.  Skipped when fewer GPUs
 are visible (the driver's single-GPU test run)."""
 import os
 import socket
@@ -59,14 +59,16 @@ def _worker(rank, world, port, cases, q_out):
     dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_sequence_sharded_two_gpus():
+@pytest.mark.parametrize("world", [2, 4])
+def test_sequence_sharded_gpus(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     cases = [(7, 1024, 8, 2, 128, 64, torch.bfloat16), (3, 768, 4, 4, 128, 64, torch.bfloat16),
              (0, 1024, 8, 2, 128, 64, torch.bfloat16), (5, 512, 4, 2, 64, 64, torch.float16)]
     ctx = mp.get_context("spawn")
     q_out = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, cases, q_out)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cases, q_out)) for r in range(world)]
     for p in procs:
         p.start()
     errs = q_out.get(timeout=600)
