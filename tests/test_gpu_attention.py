@@ -547,7 +547,7 @@ def test_key_side_tensor_core_matches_fma_kernel(esa, dtype, G, D, layer):
         assert diff.max().item() <= 1e-3, (t, diff.max().item())
 
 
-@pytest.mark.parametrize("layer", [3, 7])
+@pytest.mark.parametrize("layer", [0, 3, 7])
 def test_sequence_split_kernel_offsets(esa, layer):
     """The kernel arguments of the sequence split, on one GPU: L = 65536 split
     4 ways into virtual ranks; rank r calls ops.forward / ops.backward on its
