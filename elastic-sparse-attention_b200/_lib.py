@@ -18,6 +18,7 @@ LIB_PATH = os.path.join(_HERE, "libesa_b200.so")
 
 ESA_OK = 0
 FLAG_GATHER_ONLY = 1
+FLAG_F32_DKV = 2     # esa_backward writes dk / dv as float32
 DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 # Every symbol exported by include/esa_b200.h.

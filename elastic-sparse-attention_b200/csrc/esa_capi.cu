@@ -909,10 +909,12 @@ int esa_backward(const esa_problem_t* pb, esa_tensor_t q, esa_tensor_t k, esa_te
   if (int rc = check_problem(pb)) return rc;
   if (pb->batch == 0) return ESA_OK;
   const int es = elem_size(pb->dtype);
+  static_assert(ESA_FLAG_F32_DKV == esa::kFlagF32Dkv, "flag values");
+  const int es_dkv = (pb->flags & ESA_FLAG_F32_DKV) ? 4 : es;
   if (int rc = check_tensor("k", k, es)) return rc;
   if (int rc = check_tensor("v", v, es)) return rc;
-  if (int rc = check_tensor("dk", dk, es)) return rc;
-  if (int rc = check_tensor("dv", dv, es)) return rc;
+  if (int rc = check_tensor("dk", dk, es_dkv)) return rc;
+  if (int rc = check_tensor("dv", dv, es_dkv)) return rc;
   if (pb->q_len > 0) {
     if (int rc = check_tensor("q", q, es)) return rc;
     if (int rc = check_tensor("o", o, es)) return rc;

@@ -1134,11 +1134,25 @@ bwd_key_kernel(const AttnParams p) {
         adv[e] += __shfl_xor_sync(0xffffffffu, adv[e], o);
       }
     if (g == 0) {
-      T* dkrow = reinterpret_cast<T*>(p.dk) + b * p.sdkb + hkv * p.sdkh + (int64_t)lr * p.sdks + r * EPL;
-      T* dvrow = reinterpret_cast<T*>(p.dv) + b * p.sdvb + hkv * p.sdvh + (int64_t)lr * p.sdvs + r * EPL;
+      const int64_t ok_ = b * p.sdkb + hkv * p.sdkh + (int64_t)lr * p.sdks + r * EPL;
+      const int64_t ov_ = b * p.sdvb + hkv * p.sdvh + (int64_t)lr * p.sdvs + r * EPL;
+      // the final dK / dV row piece: input dtype, or fp32 with ESA_FLAG_F32_DKV
+      auto store = [&]() {
+        if (p.flags & kFlagF32Dkv) {
+          float* fk = reinterpret_cast<float*>(p.dk) + ok_;
+          float* fv = reinterpret_cast<float*>(p.dv) + ov_;
+#pragma unroll
+          for (int e = 0; e < EPL; e += 4) {
+            *reinterpret_cast<float4*>(fk + e) = make_float4(adk[e], adk[e + 1], adk[e + 2], adk[e + 3]);
+            *reinterpret_cast<float4*>(fv + e) = make_float4(adv[e], adv[e + 1], adv[e + 2], adv[e + 3]);
+          }
+        } else {
+          stg16(reinterpret_cast<T*>(p.dk) + ok_, V::from_float(adk));
+          stg16(reinterpret_cast<T*>(p.dv) + ov_, V::from_float(adv));
+        }
+      };
       if (p.G == 1) {
-        stg16(dkrow, V::from_float(adk));
-        stg16(dvrow, V::from_float(adv));
+        store();
       } else {
         const int64_t plane = (int64_t)p.B * p.Hkv * p.kv_rows * D;
         float* ak = p.acc + (((int64_t)b * p.Hkv + hkv) * p.kv_rows + lr) * D + r * EPL;
@@ -1153,8 +1167,7 @@ bwd_key_kernel(const AttnParams p) {
           }
         }
         if (p.head_in_group == p.G - 1) {
-          stg16(dkrow, V::from_float(adk));
-          stg16(dvrow, V::from_float(adv));
+          store();
         } else {
 #pragma unroll
           for (int e = 0; e < EPL; e += 4) {

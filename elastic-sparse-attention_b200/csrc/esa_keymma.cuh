@@ -653,10 +653,15 @@ bwd_key_mma_kernel(const AttnParams p) {
             v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
           }
           if (last) {
-            T* dst = tensor == 0
-                         ? reinterpret_cast<T*>(p.dk) + b * p.sdkb + hkv * p.sdkh + (int64_t)row * p.sdks
-                         : reinterpret_cast<T*>(p.dv) + b * p.sdvb + hkv * p.sdvh + (int64_t)row * p.sdvs;
-            *reinterpret_cast<uint2*>(dst + 4 * qd) = make_uint2(pack2<T>(v.x, v.y), pack2<T>(v.z, v.w));
+            const int64_t off = tensor == 0
+                                    ? b * p.sdkb + hkv * p.sdkh + (int64_t)row * p.sdks + 4 * qd
+                                    : b * p.sdvb + hkv * p.sdvh + (int64_t)row * p.sdvs + 4 * qd;
+            void* base = tensor == 0 ? p.dk : p.dv;
+            if (p.flags & kFlagF32Dkv)   // unrounded sums (ESA_FLAG_F32_DKV)
+              *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + off) = v;
+            else
+              *reinterpret_cast<uint2*>(reinterpret_cast<T*>(base) + off) =
+                  make_uint2(pack2<T>(v.x, v.y), pack2<T>(v.z, v.w));
           } else {
             *reinterpret_cast<float4*>(acc) = v;
           }

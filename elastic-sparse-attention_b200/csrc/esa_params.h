@@ -81,6 +81,9 @@ __device__ __forceinline__ bool dropout_keep(const AttnParams& p, int pos, int b
   return word >= p.drop_threshold;
 }
 
+// AttnParams::flags bit (ESA_FLAG_F32_DKV): dk / dv are float32 buffers.
+constexpr int kFlagF32Dkv = 2;
+
 enum ErrBits : int {
   kErrKvRange = 1,     // an index fell outside the k/v rows handed to the launch
   kErrQueryRange = 4,  // a rows[] entry outside [-kv_len, kv_len)

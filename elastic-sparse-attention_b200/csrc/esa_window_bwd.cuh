@@ -584,21 +584,30 @@ window_bwd_dkv_tc_kernel(const __grid_constant__ WindowBwdTmaps maps, const Attn
         __all_sync(0xffffffffu, sm100::mbar_wait(bar_done, 0, kWinWaitIters)) && ok && !*failed;
     sm100::tc_fence_after();
     if (ok_o) {
-      T* dkrow = reinterpret_cast<T*>(p.dk) + b * p.sdkb + hkv * p.sdkh + (int64_t)(kr0 + t) * p.sdks;
-      T* dvrow = reinterpret_cast<T*>(p.dv) + b * p.sdvb + hkv * p.sdvh + (int64_t)(kr0 + t) * p.sdvs;
+      const int64_t ok_ = b * p.sdkb + hkv * p.sdkh + (int64_t)(kr0 + t) * p.sdks;
+      const int64_t ov_ = b * p.sdvb + hkv * p.sdvh + (int64_t)(kr0 + t) * p.sdvs;
+      const bool f32 = p.flags & kFlagF32Dkv;   // unrounded sums (ESA_FLAG_F32_DKV)
+      // 32 columns of a dK or dV row: input dtype, or fp32
+      auto store32 = [&](void* base, int64_t off, const float* o) {
+        if (f32) {
+          float* dst = reinterpret_cast<float*>(base) + off;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(dst + 4 * u) = make_float4(o[4 * u], o[4 * u + 1],
+                                                                  o[4 * u + 2], o[4 * u + 3]);
+        } else {
+          T* dst = reinterpret_cast<T*>(base) + off;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) stg16(dst + u * 8, Vec<T>::from_float(o + u * 8));
+        }
+      };
 #pragma unroll
       for (int c = 0; c < kWinHeadDim / 32; ++c) {
         float o[32];
         sm100::tmem_ld_x32(tDK + lane_base + c * 32, o);
-        if (live_k) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) stg16(dkrow + c * 32 + u * 8, Vec<T>::from_float(o + u * 8));
-        }
+        if (live_k) store32(p.dk, ok_ + c * 32, o);
         sm100::tmem_ld_x32(tDV + lane_base + c * 32, o);
-        if (live_k) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) stg16(dvrow + c * 32 + u * 8, Vec<T>::from_float(o + u * 8));
-        }
+        if (live_k) store32(p.dv, ov_ + c * 32, o);
       }
     } else if (p.err) {
       atomicOr(p.err, kErrTimeout);

@@ -194,29 +194,33 @@ def backward(q, k, v, o, lse, dout, spec: PatternSpec, scale: float,
              kv_offset: int = 0, sorted_rows=None, row_perm=None, workspace=None,
              dropout_p: float = 0.0, dropout_seed: int = 0, dq=None, dk=None, dv=None,
              probs: torch.Tensor | None = None, gather_only: bool = False,
-             key_plan: torch.Tensor | None = None):
+             key_plan: torch.Tensor | None = None, dkv_fp32: bool = False):
     """Backward pass.  Returns (dq, dk, dv) in the input dtype.  With dropout,
     pass the forward's dropout_p and dropout_seed (the keep mask is rebuilt).
     dq / dk / dv may be given as (strided) views to write the gradients into,
     e.g. the q / k / v parts of one fused QKV gradient buffer.  ``gather_only``
     keeps sliding-window layers off the tensor-core backward (cross-checks).
     ``key_plan`` (from :func:`key_plan` for the same problem) spares the key
-    side its pattern searches."""
+    side its pattern searches.  ``dkv_fp32``: dk / dv are float32 (the
+    unrounded sums, for callers that add partial key gradients of several
+    calls); dq stays in the input dtype."""
     dev = _check_device(q, k, v, o, lse, dout)
+    kv_dtype = torch.float32 if dkv_fp32 else k.dtype
     dq = torch.empty_like(q) if dq is None else dq
-    dk = torch.empty_like(k) if dk is None else dk
-    dv = torch.empty_like(v) if dv is None else dv
-    for g, ref in ((dq, q), (dk, k), (dv, v)):
-        if g.shape != ref.shape or g.dtype != ref.dtype or g.device != ref.device:
-            raise ValueError("gradient buffers must match the shapes and dtypes of q, k, v")
+    dk = torch.empty_like(k, dtype=kv_dtype) if dk is None else dk
+    dv = torch.empty_like(v, dtype=kv_dtype) if dv is None else dv
+    for g, ref, dt in ((dq, q, q.dtype), (dk, k, kv_dtype), (dv, v, kv_dtype)):
+        if g.shape != ref.shape or g.dtype != dt or g.device != ref.device:
+            raise ValueError("gradient buffers must match the shapes of q, k, v and their dtypes "
+                             "(float32 for dk / dv with dkv_fp32)")
     if probs is not None:
         _check_probs(probs, q, spec)
     if key_plan is not None and (key_plan.dtype != torch.uint8 or key_plan.device != dev
                                  or not key_plan.is_contiguous()):
         raise ValueError("key_plan must be the contiguous uint8 buffer from key_plan()")
+    flags = (_lib.FLAG_GATHER_ONLY if gather_only else 0) | (_lib.FLAG_F32_DKV if dkv_fp32 else 0)
     pb = _problem(q, k, spec, scale, rows, row_offset, k.shape[2] if kv_len is None else kv_len,
-                  kv_offset, _lib.FLAG_GATHER_ONLY if gather_only else 0, dropout_p,
-                  dropout_seed, None, probs, key_plan)
+                  kv_offset, flags, dropout_p, dropout_seed, None, probs, key_plan)
     lib = _lib.load()
     need = lib.esa_backward_workspace_size(ctypes.byref(pb))
     if workspace is None or workspace.numel() < need:

@@ -127,8 +127,10 @@ class _Span:
 
 def profile_step(step, device) -> dict:
     """Runs step() once and splits this rank's device time (compute stream)
-    into kernels, waits for NCCL transfers, and the rest (layout copies,
-    fp32 sums, allocation); milliseconds."""
+    into kernels, waits for NCCL transfers, layout copies (K/V into the
+    per-group buffers, dK/dV back to [B, S, H, D]), fp32 sums of the partial
+    dK/dV, and the rest (gaps between launches, allocation, torch ops of the
+    caller); milliseconds."""
     torch.cuda.synchronize(device)
     _timing.records = []
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -142,9 +144,10 @@ def profile_step(step, device) -> dict:
         _timing.records = None
     total = e0.elapsed_time(e1)
     out = {"step_ms": round(total, 3)}
-    for kind in ("kernels", "exchange_wait"):
+    kinds = ("kernels", "exchange_wait", "layout", "reduce")
+    for kind in kinds:
         out[kind + "_ms"] = round(sum(a.elapsed_time(b) for k, a, b in recs if k == kind), 3)
-    out["other_ms"] = round(total - out["kernels_ms"] - out["exchange_wait_ms"], 3)
+    out["other_ms"] = round(total - sum(out[k + "_ms"] for k in kinds), 3)
     return out
 
 
@@ -213,10 +216,11 @@ class _ShardedFunction(torch.autograd.Function):
         rows = b0 - lo
         L = plan.world * plan.rows_per_rank
         # per head group: [rows, B, hg, D]; row slices are contiguous for the transfers
-        kbuf = torch.empty((ngroups, rows, B, hg, D), dtype=k.dtype, device=k.device)
-        vbuf = torch.empty_like(kbuf)
-        kbuf[:, a0 - lo:] = k.transpose(0, 1).reshape(S, B, ngroups, hg, D).permute(2, 0, 1, 3, 4)
-        vbuf[:, a0 - lo:] = v.transpose(0, 1).reshape(S, B, ngroups, hg, D).permute(2, 0, 1, 3, 4)
+        with _Span("layout"):
+            kbuf = torch.empty((ngroups, rows, B, hg, D), dtype=k.dtype, device=k.device)
+            vbuf = torch.empty_like(kbuf)
+            kbuf[:, a0 - lo:] = k.transpose(0, 1).reshape(S, B, ngroups, hg, D).permute(2, 0, 1, 3, 4)
+            vbuf[:, a0 - lo:] = v.transpose(0, 1).reshape(S, B, ngroups, hg, D).permute(2, 0, 1, 3, 4)
         works = [_fetch(plan, rank, group, (kbuf[g], vbuf[g]), lo) for g in range(ngroups)]
         out = torch.empty_like(q)                        # [B, S, Hq, D]
         lses, probs = [], []
@@ -258,7 +262,10 @@ class _ShardedFunction(torch.autograd.Function):
         lo = plan.lo[rank]
         L = plan.world * plan.rows_per_rank
         dq = torch.empty_like(q)
-        dkb, dvb = torch.empty_like(kbuf), torch.empty_like(vbuf)
+        # partial dK / dV in fp32: the partials of a key from several ranks
+        # are added unrounded and rounded once, as in the one-GPU key side
+        dkb = torch.empty(kbuf.shape, dtype=torch.float32, device=kbuf.device)
+        dvb = torch.empty_like(dkb)
         pending = []
         for g in range(ngroups):
             h0 = g * hg * G
@@ -270,18 +277,24 @@ class _ShardedFunction(torch.autograd.Function):
                              do[:, :, sl].transpose(1, 2), sg, scale, row_offset=a0, kv_len=L,
                              kv_offset=lo, dq=dq[:, :, sl].transpose(1, 2),
                              dk=dkb[g].permute(1, 2, 0, 3), dv=dvb[g].permute(1, 2, 0, 3),
+                             dkv_fp32=True,
                              **({"probs": probs[g]} if probs[g] is not None else {}))
             pending.append(_return_partials(plan, rank, group, (dkb[g], dvb[g]), lo))
-        # local rows: own partials plus the partials returned by higher ranks, in fp32
-        dk_acc = dkb[:, a0 - lo:].float()                # [ngroups, S, B, hg, D]
-        dv_acc = dvb[:, a0 - lo:].float()
+        # local rows: own partials plus the fp32 partials returned by higher
+        # ranks (only the rows they read, a suffix of this rank's rows)
+        dk_loc, dv_loc = dkb[:, a0 - lo:], dvb[:, a0 - lo:]   # [ngroups, S, B, hg, D]
         for g, (works, recvs) in enumerate(pending):
             _wait(works)
-            for (i, t, a, b) in recvs:
-                (dk_acc if i == 0 else dv_acc)[g, a - a0:b - a0] += t.float()
-        # [ngroups, S, B, hg, D] -> [B, S, Hkv, D]
-        dk = dk_acc.to(kbuf.dtype).permute(2, 1, 0, 3, 4).reshape(B, S, ngroups * hg, D)
-        dv = dv_acc.to(vbuf.dtype).permute(2, 1, 0, 3, 4).reshape(B, S, ngroups * hg, D)
+            with _Span("reduce"):
+                for (i, t, a, b) in recvs:
+                    (dk_loc if i == 0 else dv_loc)[g, a - a0:b - a0] += t
+        # [ngroups, S, B, hg, D] fp32 -> [B, S, Hkv, D] in the input dtype, one rounding
+        with _Span("layout"):
+            dk = torch.empty((B, S, ngroups, hg, D), dtype=kbuf.dtype, device=kbuf.device)
+            dv = torch.empty_like(dk)
+            dk.copy_(dk_loc.permute(2, 1, 0, 3, 4))
+            dv.copy_(dv_loc.permute(2, 1, 0, 3, 4))
+            dk, dv = dk.view(B, S, ngroups * hg, D), dv.view(B, S, ngroups * hg, D)
         return dq, dk, dv, None, None, None, None, None, None, None
 
 

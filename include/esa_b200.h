@@ -133,6 +133,12 @@ typedef struct {
 /* flags: run every layer on the CUDA-core gather kernels, also where the
  * tensor-core sliding-window kernel would apply (for cross-checking paths). */
 #define ESA_FLAG_GATHER_ONLY 1
+/* flags: esa_backward writes dk and dv as float32 (their esa_tensor_t strides
+ * in float elements) whatever the input dtype: the unrounded sums, for a
+ * caller that adds partial key gradients of several calls (the sequence
+ * split adds the partial dK / dV that other ranks' queries produce for its
+ * keys) and rounds once. */
+#define ESA_FLAG_F32_DKV 2
 
 /* Bits of the per-device error word that kernels set instead of faulting
  * (read and reset with esa_device_errors). */

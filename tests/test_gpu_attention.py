@@ -671,3 +671,26 @@ def test_gather_probe_modes(esa):
     assert esa.ops.device_errors() == 0
     assert lib.esa_probe_gather(4, ctypes.byref(pb), esa._lib.tensor4(k), esa._lib.tensor4(v),
                                 sink.data_ptr(), stream) == -1
+
+
+@pytest.mark.parametrize("layer,G,D,gather_only", [(5, 4, 128, False), (3, 1, 64, False),
+                                                   (0, 4, 128, False), (6, 2, 128, True)])
+def test_fp32_key_gradients(esa, layer, G, D, gather_only):
+    """ESA_FLAG_F32_DKV (``dkv_fp32``): every key-side writer (tensor-core key
+    kernel with and without fp32 sums between launches, the FMA key kernel,
+    the window layer's dK/dV kernel) writes the unrounded sums; rounded to the
+    input dtype they are the 16-bit results bit for bit, and dq is unchanged."""
+    g = torch.Generator().manual_seed(layer * 5 + G)
+    dt, Hkv, L, w = torch.bfloat16, 2, 2100, 64
+    q, do = randn(1, Hkv * G, L, D, dtype=dt, gen=g), randn(1, Hkv * G, L, D, dtype=dt, gen=g)
+    k, v = randn(1, Hkv, L, D, dtype=dt, gen=g), randn(1, Hkv, L, D, dtype=dt, gen=g)
+    spec = esa.PatternSpec(layer, 8, w)
+    scale = D ** -0.5
+    o, lse = esa.ops.forward(q, k, v, spec, scale, gather_only=gather_only)
+    dq, dk, dv = esa.ops.backward(q, k, v, o, lse, do, spec, scale, gather_only=gather_only)
+    dq32, dk32, dv32 = esa.ops.backward(q, k, v, o, lse, do, spec, scale, gather_only=gather_only,
+                                        dkv_fp32=True)
+    assert dk32.dtype == torch.float32 and dv32.dtype == torch.float32
+    assert torch.equal(dq32, dq)
+    assert torch.equal(dk32.to(dt), dk) and torch.equal(dv32.to(dt), dv)
+    assert esa.ops.device_errors() == 0

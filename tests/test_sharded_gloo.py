@@ -55,7 +55,7 @@ class OracleOps:
 
     @classmethod
     def backward(cls, q, k, v, o, lse, dout, spec, scale, rows=None, row_offset=0, kv_len=None,
-                 kv_offset=0, dq=None, dk=None, dv=None):
+                 kv_offset=0, dq=None, dk=None, dv=None, dkv_fp32=False):
         idx, mask = cls._local(q, k, spec, row_offset, kv_len, kv_offset)
         _, gq, gk, gv = naive.naive_forward_backward_manual(q, k, v, dout, idx, mask, scale,
                                                             q.shape[1] // k.shape[1])
