@@ -758,7 +758,7 @@ def incumbent_worker(path):
     save()
 
 
-def bench_c5(args, world, rank, local, steps=3, warmup=2):
+def bench_c5(args, world, rank, local, steps=5, warmup=2):
     """C5: B=1, 16 heads, D=128, L=2^20, bf16, the 8 P8 layers fwd+bwd, query
     rows (and K/V rows) split across the ranks; each rank fetches the remote
     K/V range its queries read over NCCL and returns partial dK/dV (strong
