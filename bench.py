@@ -304,6 +304,30 @@ def timed_steps(step, steps, warmup, dev, world, clocks_gpu=None):
     return ms, clocks.summary()
 
 
+def timed_steps_each(step, steps, warmup, dev, world):
+    """Like timed_steps, with CUDA events around every step: (mean ms, [ms of
+    each step, max over ranks], clock summary)."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    with ClockSampler(dev.index) as clocks:
+        torch.cuda.synchronize()
+        ev[0].record(stream)
+        for i in range(steps):
+            step()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+    each = [max_over_ranks(ev[i].elapsed_time(ev[i + 1]), dev, world) for i in range(steps)]
+    ms = max_over_ranks(ev[0].elapsed_time(ev[steps]) / steps, dev, world)
+    if world > 1:
+        torch.distributed.barrier()
+    return ms, each, clocks.summary()
+
+
 def bench_ours(args, world, rank, local):
     import elastic_sparse_attention_b200 as esa
     dev = torch.device("cuda", local)
@@ -793,7 +817,7 @@ def bench_c5(args, world, rank, local, steps=5, warmup=2):
             out = m(qq, kk, vv)
             out.backward(do)
 
-    ms, clocks = timed_steps(step, steps, warmup, dev, world)
+    ms, each, clocks = timed_steps_each(step, steps, warmup, dev, world)
     prof = esa.sharded.profile_step(step, dev)
     prof_all = [prof]
     if world > 1:
@@ -808,6 +832,7 @@ def bench_c5(args, world, rank, local, steps=5, warmup=2):
             "workload": "C5: fwd+bwd of the 8 P8 layers, B=1, 16 heads, L=2^20, D=128, bf16, "
                         "query rows split over the ranks, remote K/V fetched with NCCL",
             "rows_per_rank": S, "max_rows_fetched_per_layer_per_rank": fetched,
+            "step_ms_each": [round(x, 1) for x in each],
             "per_rank_ms": prof_all, "clocks": clocks}
 
 
