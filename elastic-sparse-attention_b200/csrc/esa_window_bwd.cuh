@@ -13,9 +13,9 @@
 //            UMMA 2  dP = dO V^T               TMEM stage [128, 128 + NK)
 //            UMMA 3  dQ = dS K                 TMEM stage [0, 128) (S is read by then)
 //            issued in whichever order their inputs become ready (polling)
-//   warps 0-3 / 4-7 (one warpgroup per stage, one row per thread): delta =
-//            rowsum(dO o O) and lse from global while the MMAs run (delta is
-//            stored for the second kernel); P = exp2(S * scale_log2 - lse),
+//   warps 0-3 / 4-7 (one warpgroup per stage, one row per thread): P =
+//            exp2(S * scale_log2 - lse) from TMEM, delta = sum_k P_k dP_k (equal
+//            to rowsum(dO o O) for the exact O; stored for the second kernel),
 //            dS = P (dP - delta) * scale, dS (input type) over the tile's Q in
 //            SMEM, K-major over keys; then the tile's epilogue (dQ -> global).
 //
@@ -253,46 +253,49 @@ window_bwd_dq_tc_kernel(const __grid_constant__ WindowBwdTmaps maps, const AttnP
       const int pos = p.row_offset + j;
       const int lo = max(0, pos - p.pat.w + 1) - tl.ks;   // valid key columns [lo, hi]
       const int hi = pos - tl.ks;
-      // delta = rowsum(dO o O) and lse while the loads and UMMAs run
-      float delta = 0.f, lse = 0.f;
-      if (live) {
-        const T* orow =
-            reinterpret_cast<const T*>(p.o) + tl.b * p.sob + h * p.soh + (int64_t)j * p.sos;
-        const T* drow = reinterpret_cast<const T*>(p.dout) + tl.b * p.sdob + h * p.sdoh +
-                        (int64_t)j * p.sdos;
-#pragma unroll 4
-        for (int c = 0; c < kWinHeadDim / 8; ++c)
-          delta = Mix<T>::dot(ldg16(orow + c * 8), ldg16(drow + c * 8), delta);
-        const int64_t ix = ((int64_t)tl.b * p.Hq + h) * p.n_rows + j;
-        lse = p.lse[ix];
-        delta_out[ix] = delta;
-      }
+      const int64_t ix = ((int64_t)tl.b * p.Hq + h) * p.n_rows + j;
+      const float lse = live ? p.lse[ix] : 0.f;
       ok = ok && __all_sync(0xffffffffu, sm100::mbar_wait(sd_ready + s, ph, kWinWaitIters)) &&
            !*failed;
       sm100::tc_fence_after();
       if (ok) {
-        const int nch = (nk + 31) / 32;
-        for (int cc = 0; cc < nch; ++cc) {
-          float sc[32], dp[32];
-          sm100::tmem_ld_x32(tmem + s * 256 + lane_base + cc * 32, sc);
-          sm100::tmem_ld_x32(tmem + s * 256 + 128 + lane_base + cc * 32, dp);
+        // two passes over the row's S / dP in TMEM, 32 keys at a time: the row
+        // value delta = sum_k P_k dP_k with P = exp2(S * scale_log2 - lse)
+        // (rowsum(dO o O) for the exact O: no O read, and no rounding of the
+        // stored 16-bit O, which shows in dK of keys with few users), then
+        // dS = P (dP - delta) * scale
+        constexpr int kCh = kWbqMaxKeys / 32;
+        float delta = 0.f;
 #pragma unroll
-          for (int u8 = 0; u8 < 4; ++u8) {
-            const int c8 = cc * 4 + u8;   // 8-key unit
-            if (c8 * 8 >= nk) break;
-            float ds[8];
+        for (int pass = 0; pass < 2; ++pass) {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int c = c8 * 8 + u;
-              const bool valid = live && c >= lo && c <= hi;
-              const float pr = valid ? exp2f(sc[u8 * 8 + u] * p.scale_log2 - lse) : 0.f;
-              ds[u] = pr * (dp[u8 * 8 + u] - delta) * p.scale;
+          for (int cc = 0; cc < kCh; ++cc) {
+            if (cc * 32 < nk) {
+              float sc[32], dp[32];
+              sm100::tmem_ld_x32(tmem + s * 256 + lane_base + cc * 32, sc);
+              sm100::tmem_ld_x32(tmem + s * 256 + 128 + lane_base + cc * 32, dp);
+#pragma unroll
+              for (int u8 = 0; u8 < 4; ++u8) {
+                const int c8 = cc * 4 + u8;   // 8-key unit
+                float ds[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  const int c = c8 * 8 + u;
+                  const bool valid = live && c < nk && c >= lo && c <= hi;
+                  const float pr = valid ? exp2f(sc[u8 * 8 + u] * p.scale_log2 - lse) : 0.f;
+                  if (pass == 0) delta += pr * dp[u8 * 8 + u];
+                  else ds[u] = pr * (dp[u8 * 8 + u] - delta) * p.scale;
+                }
+                if (pass == 1 && c8 * 8 < nk) {
+                  const int chunk = c8 >> 3, unit = c8 & 7;
+                  unsigned char* dst =
+                      sQ(s) + chunk * (kWinRows * 128) + t * 128 + ((unit ^ (t & 7)) << 4);
+                  *reinterpret_cast<uint4*>(dst) = Vec<T>::from_float(ds);
+                }
+              }
             }
-            const int chunk = c8 >> 3, unit = c8 & 7;
-            unsigned char* dst =
-                sQ(s) + chunk * (kWinRows * 128) + t * 128 + ((unit ^ (t & 7)) << 4);
-            *reinterpret_cast<uint4*>(dst) = Vec<T>::from_float(ds);
           }
+          if (pass == 0 && live) delta_out[ix] = delta;
         }
       }
       sm100::fence_async_smem();

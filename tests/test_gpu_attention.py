@@ -694,3 +694,10 @@ def test_fp32_key_gradients(esa, layer, G, D, gather_only):
     assert torch.equal(dq32, dq)
     assert torch.equal(dk32.to(dt), dk) and torch.equal(dv32.to(dt), dv)
     assert esa.ops.device_errors() == 0
+
+
+def test_graft_smoke(esa):
+    """The repository's smoke check (module forward + backward of a dilated
+    and the sliding-window layer against the oracle) as part of the suite."""
+    import __graft_entry__
+    __graft_entry__.smoke()
