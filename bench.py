@@ -817,8 +817,16 @@ def bench_c5(args, world, rank, local, steps=5, warmup=2):
             out = m(qq, kk, vv)
             out.backward(do)
 
+    stats0 = torch.cuda.memory_stats(dev)
     ms, each, clocks = timed_steps_each(step, steps, warmup, dev, world)
+    stats1 = torch.cuda.memory_stats(dev)
+    # caching-allocator activity during warm-up and timing (a retry frees the
+    # cache and synchronises the device; device allocations map new memory)
+    alloc = {k: stats1.get(k, 0) - stats0.get(k, 0)
+             for k in ("num_alloc_retries", "num_device_alloc", "num_device_free")}
+    alloc["peak_gb"] = round(stats1.get("allocated_bytes.all.peak", 0) / 1e9, 1)
     prof = esa.sharded.profile_step(step, dev)
+    prof["allocator"] = alloc
     prof_all = [prof]
     if world > 1:
         prof_all = [None] * world

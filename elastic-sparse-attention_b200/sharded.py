@@ -326,6 +326,9 @@ class SequenceShardedElasticSparseAttention(torch.nn.Module):
         self.group = group
         self.ops = ops
         self.head_groups = group_count(self.num_key_value_heads, head_groups)
+        # the key plan of the one-rank path (a group of one)
+        from .attention import KeyPlanCache
+        self.key_plans = KeyPlanCache()
 
     def plan(self, rows_per_rank: int, device) -> ShardPlan:
         world = dist.get_world_size(self.group)
@@ -340,6 +343,20 @@ class SequenceShardedElasticSparseAttention(torch.nn.Module):
             raise ValueError(f"sequence length {S * world} exceeds max_seq_len {self.max_seq_len}")
         if Hq != self.num_attention_heads or k.shape[2] != self.num_key_value_heads:
             raise ValueError("head counts of q / k do not match the module")
+        if world == 1 and self.ops is cuda_ops:
+            # nothing to exchange: the one-GPU path on the [B, S, H, D] shards
+            # read in place (no per-group buffers), with the layer's key plan
+            from .attention import ElasticSparseAttentionFunction, _forward_without_grad
+            G = Hq // k.shape[2]
+            qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+            if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad
+                                            or v.requires_grad):
+                o = ElasticSparseAttentionFunction.apply(qt, kt, vt, self.spec, self.scaling, G,
+                                                         None, 0.0, 0, False, self.key_plans)
+            else:
+                o = _forward_without_grad(qt, kt, vt, self.spec, self.scaling, G, None, 0.0, 0,
+                                          False)
+            return o.transpose(1, 2).reshape(B, S, Hq * D)
         plan = self.plan(S, q.device)
         if self.ops is cuda_ops and torch.is_grad_enabled():
             from .attention import _ensure_monotone

@@ -190,3 +190,40 @@ def test_sequence_sharded_gloo_ranks_on_one_gpu(world, case):
         assert p.exitcode == 0
     bad = [(t, mx, mean) for t, (ok, mx, mean) in zip(("out", "dq", "dk", "dv"), errs) if not ok]
     assert not bad, (case, bad)
+
+
+def _one_rank_worker(port, q_out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    import elastic_sparse_attention_b200 as esa
+    g = torch.Generator().manual_seed(9)
+    B, L, Hq, Hkv, D, dt = 1, 3000, 8, 2, 128, torch.bfloat16
+    q, k, v = (torch.randn(B, L, h, D, generator=g).to(DEV_ONE, dt) for h in (Hq, Hkv, Hkv))
+    do = torch.randn(B, L, Hq * D, generator=g).to(DEV_ONE, dt)
+    res = []
+    for mk in (lambda: esa.SequenceShardedElasticSparseAttention(5, 8, Hq, D, 64, L,
+                                                                 num_key_value_heads=Hkv),
+               lambda: esa.ElasticSparseAttention(5, 8, Hq, D, 64, L, num_key_value_heads=Hkv)):
+        m = mk()
+        qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
+        if isinstance(m, esa.ElasticSparseAttention):
+            out, _ = m(qq.transpose(1, 2), kk.transpose(1, 2), vv.transpose(1, 2))
+        else:
+            out = m(qq, kk, vv)
+        out.backward(do)
+        res.append([out.detach(), qq.grad, kk.grad, vv.grad])
+    q_out.put([bool(torch.equal(a, b)) for a, b in zip(*res)])
+    dist.destroy_process_group()
+
+
+def test_sequence_sharded_one_rank_is_the_module():
+    """A sequence group of one rank runs the one-GPU path: outputs and
+    gradients equal those of ElasticSparseAttention on the same tensors."""
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    p = ctx.Process(target=_one_rank_worker, args=(_port(), q_out))
+    p.start()
+    same = q_out.get(timeout=300)
+    p.join(timeout=60)
+    assert p.exitcode == 0
+    assert all(same), same
