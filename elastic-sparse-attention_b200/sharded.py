@@ -34,6 +34,7 @@ attention layer produces), read in place by the kernels through strides.
 from __future__ import annotations
 
 import threading
+import time
 from dataclasses import dataclass
 
 import torch
@@ -102,6 +103,7 @@ def make_plan(num_heads: int, spec: PatternSpec, rows_per_rank: int, world: int,
 # ---------------------------------------------------------------------------
 class _Timing:
     records = None
+    host_ms = None   # host time spent issuing NCCL batches (dict), while profiling
 
 
 _timing = _Timing()
@@ -133,17 +135,25 @@ def profile_step(step, device) -> dict:
     caller); milliseconds."""
     torch.cuda.synchronize(device)
     _timing.records = []
+    _timing.host_ms = {"nccl_issue": 0.0}
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     try:
         e0.record()
+        t0 = time.perf_counter()
         step()
+        host = (time.perf_counter() - t0) * 1e3
         e1.record()
         torch.cuda.synchronize(device)
         recs = _timing.records
+        nccl_issue = _timing.host_ms["nccl_issue"]
     finally:
         _timing.records = None
+        _timing.host_ms = None
     total = e0.elapsed_time(e1)
-    out = {"step_ms": round(total, 3)}
+    # host_ms: the host's time to issue the step (close to step_ms means the
+    # GPU waited for the host); nccl_issue_host_ms: of it, inside NCCL calls
+    out = {"step_ms": round(total, 3), "host_ms": round(host, 3),
+           "nccl_issue_host_ms": round(nccl_issue, 3)}
     kinds = ("kernels", "exchange_wait", "layout", "reduce")
     for kind in kinds:
         out[kind + "_ms"] = round(sum(a.elapsed_time(b) for k, a, b in recs if k == kind), 3)
@@ -153,7 +163,14 @@ def profile_step(step, device) -> dict:
 
 def _batch(p2p):
     """Issue one grouped batch of point-to-point operations; [] if none."""
-    return dist.batch_isend_irecv(p2p) if p2p else []
+    if not p2p:
+        return []
+    if _timing.host_ms is None:
+        return dist.batch_isend_irecv(p2p)
+    t0 = time.perf_counter()
+    works = dist.batch_isend_irecv(p2p)
+    _timing.host_ms["nccl_issue"] += (time.perf_counter() - t0) * 1e3
+    return works
 
 
 def _wait(works):
