@@ -816,6 +816,11 @@ def bench_c5(args, world, rank, local, steps=5, warmup=2):
         for m in mods:
             out = m(qq, kk, vv)
             out.backward(do)
+        # the host waits for its step before issuing the next, as a training
+        # loop that reads its loss does: without it a rank whose host runs
+        # ahead queues the NCCL transfers of later steps behind the current
+        # ones (steps of 4-12 s were seen at 2 ranks, against 0.78 s here)
+        torch.cuda.current_stream().synchronize()
 
     stats0 = torch.cuda.memory_stats(dev)
     ms, each, clocks = timed_steps_each(step, steps, warmup, dev, world)
