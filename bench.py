@@ -830,6 +830,7 @@ def bench_c5(args, world, rank, local, steps=5, warmup=2):
     alloc = {k: stats1.get(k, 0) - stats0.get(k, 0)
              for k in ("num_alloc_retries", "num_device_alloc", "num_device_free")}
     alloc["peak_gb"] = round(stats1.get("allocated_bytes.all.peak", 0) / 1e9, 1)
+    alloc["reserved_peak_gb"] = round(stats1.get("reserved_bytes.all.peak", 0) / 1e9, 1)
     prof = esa.sharded.profile_step(step, dev)
     prof["allocator"] = alloc
     prof_all = [prof]
