@@ -46,6 +46,28 @@ from .ops import PatternSpec
 _plan_lock = threading.Lock()
 _plan_cache: dict = {}
 
+# One scratch buffer per device for the backward's temporaries (the fp32
+# partial dK / dV of the buffer rows and the kernels' workspace): the layers'
+# backwards run one after another and each ends by waiting for its transfers,
+# so they can share it, and the caching allocator does not have to find room
+# for ~10 GB of differently sized blocks per layer.
+_scratch_lock = threading.Lock()
+_scratch: dict = {}
+
+
+def _scratch_bytes(device: torch.device, nbytes: int) -> torch.Tensor:
+    """A uint8 buffer of at least nbytes on device (256-byte aligned start),
+    shared by every sequence-sharded backward on that device."""
+    nbytes = (nbytes + 255) // 256 * 256
+    with _scratch_lock:
+        buf = _scratch.get(device)
+        if buf is None or buf.numel() < nbytes:
+            _scratch.pop(device, None)
+            del buf
+            buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            _scratch[device] = buf
+        return buf
+
 
 @dataclass(frozen=True)
 class ShardPlan:
@@ -280,9 +302,18 @@ class _ShardedFunction(torch.autograd.Function):
         L = plan.world * plan.rows_per_rank
         dq = torch.empty_like(q)
         # partial dK / dV in fp32: the partials of a key from several ranks
-        # are added unrounded and rounded once, as in the one-GPU key side
-        dkb = torch.empty(kbuf.shape, dtype=torch.float32, device=kbuf.device)
-        dvb = torch.empty_like(dkb)
+        # are added unrounded and rounded once, as in the one-GPU key side;
+        # they and the kernels' workspace live in the device's shared scratch
+        nkv = kbuf.numel()
+        g_q = q[:, :, :hg * G].transpose(1, 2)
+        g_k = kbuf[0].permute(1, 2, 0, 3)
+        ws_bytes = (ops.backward_workspace_bytes(g_q, g_k, spec, kv_len=L)
+                    if hasattr(ops, "backward_workspace_bytes") else 0)
+        ws_bytes = (ws_bytes + 255) // 256 * 256
+        scratch = _scratch_bytes(kbuf.device, 2 * nkv * 4 + ws_bytes)
+        dkb = scratch[:nkv * 4].view(torch.float32).view(kbuf.shape)
+        dvb = scratch[nkv * 4:2 * nkv * 4].view(torch.float32).view(kbuf.shape)
+        ws = scratch[2 * nkv * 4:2 * nkv * 4 + ws_bytes] if ws_bytes else None
         pending = []
         for g in range(ngroups):
             h0 = g * hg * G
@@ -295,7 +326,8 @@ class _ShardedFunction(torch.autograd.Function):
                              kv_offset=lo, dq=dq[:, :, sl].transpose(1, 2),
                              dk=dkb[g].permute(1, 2, 0, 3), dv=dvb[g].permute(1, 2, 0, 3),
                              dkv_fp32=True,
-                             **({"probs": probs[g]} if probs[g] is not None else {}))
+                             **({"probs": probs[g]} if probs[g] is not None else {}),
+                             **({"workspace": ws} if ws is not None else {}))
             pending.append(_return_partials(plan, rank, group, (dkb[g], dvb[g]), lo))
         # local rows: own partials plus the fp32 partials returned by higher
         # ranks (only the rows they read, a suffix of this rank's rows)
