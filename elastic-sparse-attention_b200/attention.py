@@ -72,13 +72,19 @@ class KeyPlanCache:
         self._key = None
         self._plan = None
 
-    def get(self, q: torch.Tensor, k: torch.Tensor, spec: PatternSpec) -> Optional[torch.Tensor]:
+    def get(self, q: torch.Tensor, k: torch.Tensor, spec: PatternSpec, row_offset: int = 0,
+            kv_len: Optional[int] = None, kv_offset: int = 0,
+            build=None) -> Optional[torch.Tensor]:
+        """The plan for these shapes and offsets (``build``: the function that
+        makes it, :func:`ops.key_plan` by default)."""
         if not self.enabled:
             return None
-        key = (q.device, q.dtype, tuple(q.shape[1:]), tuple(k.shape[1:3]), spec)
+        key = (q.device, q.dtype, tuple(q.shape[1:]), tuple(k.shape[1:3]), spec, row_offset,
+               kv_len, kv_offset)
         if key != self._key:
             self._key, self._plan = None, None   # release the old plan first
-            self._plan = ops.key_plan(q, k, spec)
+            self._plan = (build or ops.key_plan)(q, k, spec, row_offset=row_offset,
+                                                 kv_len=kv_len, kv_offset=kv_offset)
             self._key = key
         return self._plan
 

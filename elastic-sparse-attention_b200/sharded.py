@@ -244,7 +244,7 @@ def group_count(num_kv_heads: int, wanted: int) -> int:
 class _ShardedFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, spec: PatternSpec, scale: float, plan: ShardPlan, rank: int,
-                group, ops, ngroups: int):
+                group, ops, ngroups: int, key_plans=None):
         # q [B, S, Hq, D], k/v [B, S, Hkv, D] (sequence-major shards)
         B, S, Hq, D = q.shape
         Hkv = k.shape[2]
@@ -282,6 +282,7 @@ class _ShardedFunction(torch.autograd.Function):
                               *[p for p in probs if p is not None])
         ctx.has_probs = [p is not None for p in probs]
         ctx.meta = (spec, scale, plan, rank, group, ops, ngroups)
+        ctx.key_plans = key_plans if hasattr(ops, "key_plan") else None
         return out
 
     @staticmethod
@@ -319,6 +320,12 @@ class _ShardedFunction(torch.autograd.Function):
             h0 = g * hg * G
             sl = slice(h0, h0 + hg * G)
             sg = spec.heads(Hq, h0)
+            # the group's key plan (built at the first backward of this shape)
+            kp = None
+            if ctx.key_plans is not None:
+                kp = ctx.key_plans[g].get(q[:, :, sl].transpose(1, 2), kbuf[g].permute(1, 2, 0, 3),
+                                          sg, row_offset=a0, kv_len=L, kv_offset=lo,
+                                          build=ops.key_plan)
             with _Span("kernels"):
                 ops.backward(q[:, :, sl].transpose(1, 2), kbuf[g].permute(1, 2, 0, 3),
                              vbuf[g].permute(1, 2, 0, 3), out[:, :, sl].transpose(1, 2), lses[g],
@@ -327,7 +334,8 @@ class _ShardedFunction(torch.autograd.Function):
                              dk=dkb[g].permute(1, 2, 0, 3), dv=dvb[g].permute(1, 2, 0, 3),
                              dkv_fp32=True,
                              **({"probs": probs[g]} if probs[g] is not None else {}),
-                             **({"workspace": ws} if ws is not None else {}))
+                             **({"workspace": ws} if ws is not None else {}),
+                             **({"key_plan": kp} if kp is not None else {}))
             pending.append(_return_partials(plan, rank, group, (dkb[g], dvb[g]), lo))
         # local rows: own partials plus the fp32 partials returned by higher
         # ranks (only the rows they read, a suffix of this rank's rows)
@@ -344,7 +352,7 @@ class _ShardedFunction(torch.autograd.Function):
             dk.copy_(dk_loc.permute(2, 1, 0, 3, 4))
             dv.copy_(dv_loc.permute(2, 1, 0, 3, 4))
             dk, dv = dk.view(B, S, ngroups * hg, D), dv.view(B, S, ngroups * hg, D)
-        return dq, dk, dv, None, None, None, None, None, None, None
+        return dq, dk, dv, None, None, None, None, None, None, None, None
 
 
 class SequenceShardedElasticSparseAttention(torch.nn.Module):
@@ -375,9 +383,11 @@ class SequenceShardedElasticSparseAttention(torch.nn.Module):
         self.group = group
         self.ops = ops
         self.head_groups = group_count(self.num_key_value_heads, head_groups)
-        # the key plan of the one-rank path (a group of one)
+        # key plans: of the one-rank path (a group of one), and of each head
+        # group's backward call in the split
         from .attention import KeyPlanCache
         self.key_plans = KeyPlanCache()
+        self.group_key_plans = [KeyPlanCache() for _ in range(self.head_groups)]
 
     def plan(self, rows_per_rank: int, device) -> ShardPlan:
         world = dist.get_world_size(self.group)
@@ -411,5 +421,5 @@ class SequenceShardedElasticSparseAttention(torch.nn.Module):
             from .attention import _ensure_monotone
             _ensure_monotone(Hq, self.spec, max(S * world, 2), q.device)
         out = _ShardedFunction.apply(q, k, v, self.spec, self.scaling, plan, rank, self.group,
-                                     self.ops, self.head_groups)
+                                     self.ops, self.head_groups, self.group_key_plans)
         return out.reshape(B, S, Hq * D)

@@ -114,13 +114,19 @@ class _CudaKernelsOnCpuTensors:
         return o, lse.cpu()
 
     @classmethod
+    def key_plan(cls, q, k, spec, row_offset=0, kv_len=None, kv_offset=0):
+        esa = cls._esa()
+        return esa.ops.key_plan(q.contiguous().to(DEV_ONE), k.contiguous().to(DEV_ONE), spec,
+                                row_offset=row_offset, kv_len=kv_len, kv_offset=kv_offset)
+
+    @classmethod
     def backward(cls, q, k, v, o, lse, dout, spec, scale, rows=None, row_offset=0, kv_len=None,
-                 kv_offset=0, dq=None, dk=None, dv=None, dkv_fp32=False):
+                 kv_offset=0, dq=None, dk=None, dv=None, dkv_fp32=False, key_plan=None):
         esa = cls._esa()
         qd, kd, vd, od, dod = (t.contiguous().to(DEV_ONE) for t in (q, k, v, o, dout))
         res = esa.ops.backward(qd, kd, vd, od, lse.to(DEV_ONE), dod, spec, scale,
                                row_offset=row_offset, kv_len=kv_len, kv_offset=kv_offset,
-                               dkv_fp32=dkv_fp32)
+                               dkv_fp32=dkv_fp32, key_plan=key_plan)
         out = []
         for got, buf in zip(res, (dq, dk, dv)):
             got = got.cpu()
