@@ -27,7 +27,7 @@ EXPORTED = ("esa_version", "esa_last_error", "esa_device_errors", "esa_forward_w
             "esa_pattern_audit", "esa_forward", "esa_backward_workspace_size", "esa_backward",
             "esa_key_plan_size", "esa_key_plan_build",
             "esa_backward_noalloc", "esa_trace_enable", "esa_trace_count", "esa_trace_read",
-            "esa_probe_gather",
+            "esa_probe_gather", "esa_copy_rows",
             # decoder-layer harness (include/esa_layer.h)
             "esa_rmsnorm_forward", "esa_rmsnorm_backward_workspace_size", "esa_rmsnorm_backward",
             "esa_rope_apply", "esa_swiglu_forward", "esa_swiglu_backward")
@@ -42,6 +42,13 @@ DEVERR_PLAN = 8
 class EsaTensor(ctypes.Structure):
     _fields_ = [("data", ctypes.c_void_p), ("stride_b", ctypes.c_int64),
                 ("stride_h", ctypes.c_int64), ("stride_s", ctypes.c_int64)]
+
+
+class EsaRows(ctypes.Structure):
+    _fields_ = [("src", ctypes.c_void_p), ("dst", ctypes.c_void_p),
+                ("src_dtype", ctypes.c_int32), ("dst_dtype", ctypes.c_int32),
+                ("row_elems", ctypes.c_int64), ("count", ctypes.c_int64 * 3),
+                ("src_stride", ctypes.c_int64 * 3), ("dst_stride", ctypes.c_int64 * 3)]
 
 
 class EsaProblem(ctypes.Structure):
@@ -116,6 +123,8 @@ def load() -> ctypes.CDLL:
         lib.esa_probe_gather.argtypes = [i32, ctypes.POINTER(EsaProblem), EsaTensor, EsaTensor,
                                          P, P]
         lib.esa_probe_gather.restype = ctypes.c_int
+        lib.esa_copy_rows.argtypes = [ctypes.POINTER(EsaRows), P]
+        lib.esa_copy_rows.restype = ctypes.c_int
         F = ctypes.c_float
         lib.esa_rmsnorm_forward.argtypes = [i32, i64, i32, P, P, P, P, F, P, P, P]
         lib.esa_rmsnorm_forward.restype = ctypes.c_int

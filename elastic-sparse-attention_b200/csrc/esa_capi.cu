@@ -26,6 +26,7 @@
 #include "esa_pattern.cuh"
 #include "esa_keyplan.cuh"
 #include "esa_probe.cuh"
+#include "esa_rows.cuh"
 #include "esa_window_tc.cuh"
 #include "esa_window_bwd.cuh"
 
@@ -1260,3 +1261,68 @@ int esa_swiglu_backward(int32_t dtype, int64_t n_rows, int32_t ffn, const void* 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// esa_copy_rows: the sequence split's layout copies (esa_rows.cuh).
+// ---------------------------------------------------------------------------
+extern "C" int esa_copy_rows(const esa_rows_t* r, void* stream) {
+  if (!r) return fail(ESA_ERR_INVALID, "esa_copy_rows: null descriptor");
+  const bool copy16 = r->src_dtype == r->dst_dtype &&
+                      (r->src_dtype == ESA_DTYPE_BF16 || r->src_dtype == ESA_DTYPE_F16);
+  const bool cast = r->src_dtype == ESA_DTYPE_F32 &&
+                    (r->dst_dtype == ESA_DTYPE_BF16 || r->dst_dtype == ESA_DTYPE_F16);
+  if (!copy16 && !cast)
+    return fail(ESA_ERR_UNSUPPORTED, "esa_copy_rows: dtypes %d -> %d (a 16-bit copy or fp32 -> "
+                "16-bit only)", r->src_dtype, r->dst_dtype);
+  if (r->row_elems <= 0 || r->row_elems % 8 || r->row_elems / 8 > INT32_MAX)
+    return fail(ESA_ERR_INVALID, "esa_copy_rows: row_elems %lld is not a positive multiple of 8",
+                (long long)r->row_elems);
+  const int64_t es = cast ? 4 : 2;
+  int64_t rows = 1;
+  for (int k = 0; k < 3; ++k) {
+    if (r->count[k] < 0 || r->src_stride[k] < 0 || r->dst_stride[k] < 0)
+      return fail(ESA_ERR_INVALID, "esa_copy_rows: negative count or stride at level %d", k);
+    if ((r->src_stride[k] * es) % 16 || (r->dst_stride[k] * 2) % 16)
+      return fail(ESA_ERR_INVALID, "esa_copy_rows: strides of level %d are not 16-byte multiples",
+                  k);
+    if (r->count[k] == 0) return ESA_OK;
+    if (rows > INT64_MAX / r->count[k])
+      return fail(ESA_ERR_INVALID, "esa_copy_rows: too many rows");
+    rows *= r->count[k];
+  }
+  if (!r->src || !r->dst || !aligned16(r->src) || !aligned16(r->dst))
+    return fail(ESA_ERR_INVALID, "esa_copy_rows: null or misaligned pointer");
+  esa::RowCopyParams p;
+  p.src = r->src;
+  p.dst = r->dst;
+  p.n0 = r->count[0];
+  p.n1 = r->count[1];
+  p.n2 = r->count[2];
+  p.s0 = r->src_stride[0];
+  p.s1 = r->src_stride[1];
+  p.s2 = r->src_stride[2];
+  p.d0 = r->dst_stride[0];
+  p.d1 = r->dst_stride[1];
+  p.d2 = r->dst_stride[2];
+  p.rows = rows;
+  p.row_vecs = (int32_t)(r->row_elems / 8);
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  // whole waves of 8-warp CTAs, 8 per SM (64 warps), each warp striding over rows
+  const int64_t ctas = std::min<int64_t>((rows + esa::kRowCopyWarps - 1) / esa::kRowCopyWarps,
+                                         (int64_t)sms * 8);
+  cudaStream_t s = (cudaStream_t)stream;
+  LaunchTrace tr("copy_rows", s);
+  const dim3 grid((unsigned)ctas), block(esa::kRowCopyWarps * 32);
+  if (copy16) {
+    if (r->src_dtype == ESA_DTYPE_BF16)
+      esa::copy_rows_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, block, 0, s>>>(p);
+    else
+      esa::copy_rows_kernel<__half, __half><<<grid, block, 0, s>>>(p);
+  } else if (r->dst_dtype == ESA_DTYPE_BF16) {
+    esa::copy_rows_kernel<float, __nv_bfloat16><<<grid, block, 0, s>>>(p);
+  } else {
+    esa::copy_rows_kernel<float, __half><<<grid, block, 0, s>>>(p);
+  }
+  return check_launch("esa_copy_rows");
+}

@@ -246,3 +246,29 @@ def _check_probs(probs: torch.Tensor, q: torch.Tensor, spec: PatternSpec) -> Non
 def backward_workspace_bytes(q, k, spec: PatternSpec, kv_len: int | None = None) -> int:
     pb = _problem(q, k, spec, 1.0, None, 0, k.shape[2] if kv_len is None else kv_len, 0)
     return int(_lib.load().esa_backward_workspace_size(ctypes.byref(pb)))
+
+
+def copy_rows(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    """``dst.copy_(src)`` for two 4-D views [n0, n1, n2, row] of the same shape
+    whose last dimension is contiguous (``esa_copy_rows``): a 16-bit copy, or
+    fp32 ``src`` rounded to a 16-bit ``dst``.  The sequence split moves its K /
+    V rows and partial dK / dV between [B, S, H, D] tensors and per-head-group
+    [rows, B, heads, D] buffers with it.  Returns ``dst``."""
+    if dst.dim() != 4 or src.shape != dst.shape:
+        raise ValueError(f"copy_rows: 4-D views of one shape expected, got {tuple(src.shape)} "
+                         f"-> {tuple(dst.shape)}")
+    if src.stride(-1) != 1 or dst.stride(-1) != 1:
+        raise ValueError("copy_rows: the last dimension must be contiguous")
+    dev = _check_device(dst, src)
+    if dst.numel() == 0:
+        return dst
+    r = _lib.EsaRows()
+    r.src, r.dst = src.data_ptr(), dst.data_ptr()
+    r.src_dtype, r.dst_dtype = _lib.DTYPES[src.dtype], _lib.DTYPES[dst.dtype]
+    r.row_elems = src.shape[3]
+    for i in range(3):
+        r.count[i], r.src_stride[i], r.dst_stride[i] = src.shape[i], src.stride(i), dst.stride(i)
+    with _on(dev):
+        _lib.check(_lib.load().esa_copy_rows(ctypes.byref(r), _lib.stream_handle(dev)),
+                   "esa_copy_rows")
+    return dst

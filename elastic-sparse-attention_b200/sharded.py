@@ -216,21 +216,45 @@ def _fetch(plan: ShardPlan, rank: int, group, bufs, lo: int):
     return _batch(p2p)
 
 
-def _return_partials(plan: ShardPlan, rank: int, group, dbufs, lo: int):
+def _return_partials(plan: ShardPlan, rank: int, group, dbufs, lo: int, space=None):
     """Issue the sends of the partial gradients of remote rows (rows below
     r*S of each buffer in dbufs) to their owners and the receives of the
     partials of this rank's rows from higher ranks; returns (works, [(buffer
-    index, tensor, start, stop)] of the receives)."""
+    index, tensor, start, stop)] of the receives).  The receives are carved
+    from ``space`` (a flat tensor of the buffers' dtype, ``len(dbufs)`` x the
+    rows of pieces_sent x a buffer row) when given, else allocated."""
     p2p, recvs = [], []
+    used = 0
     for i, dbuf in enumerate(dbufs):
         for (q, a, b) in plan.pieces_needed(rank):
             p2p.append(dist.P2POp(dist.isend, dbuf[a - lo:b - lo], group=group, group_peer=q))
         for (r, a, b) in plan.pieces_sent(rank):
-            t = torch.empty((b - a,) + tuple(dbuf.shape[1:]), dtype=dbuf.dtype,
-                            device=dbuf.device)
+            shape = (b - a,) + tuple(dbuf.shape[1:])
+            if space is None:
+                t = torch.empty(shape, dtype=dbuf.dtype, device=dbuf.device)
+            else:
+                n = (b - a) * dbuf[0].numel()
+                t = space[used:used + n].view(shape)
+                used += n
             recvs.append((i, t, a, b))
             p2p.append(dist.P2POp(dist.irecv, t, group=group, group_peer=r))
     return _batch(p2p), recvs
+
+
+def _copy_rows(ops, dst: torch.Tensor, src: torch.Tensor) -> None:
+    """dst.copy_(src) for [n0, n1, n2, row] views: the library's row-copy
+    kernel (16-byte vectors, HBM-bound) when ``ops`` has it and the views are
+    16-byte aligned; torch's strided copy otherwise (kernel-less test ops, or
+    odd caller tensors)."""
+    es_s, es_d = src.element_size(), dst.element_size()
+    if (hasattr(ops, "copy_rows") and src.is_cuda and src.stride(-1) == 1
+            and dst.stride(-1) == 1 and src.shape[-1] % 8 == 0
+            and src.data_ptr() % 16 == 0 and dst.data_ptr() % 16 == 0
+            and all((st * es_s) % 16 == 0 for st in src.stride()[:3])
+            and all((st * es_d) % 16 == 0 for st in dst.stride()[:3])):
+        ops.copy_rows(dst, src)
+    else:
+        dst.copy_(src)
 
 
 def group_count(num_kv_heads: int, wanted: int) -> int:
@@ -258,8 +282,10 @@ class _ShardedFunction(torch.autograd.Function):
         with _Span("layout"):
             kbuf = torch.empty((ngroups, rows, B, hg, D), dtype=k.dtype, device=k.device)
             vbuf = torch.empty_like(kbuf)
-            kbuf[:, a0 - lo:] = k.transpose(0, 1).reshape(S, B, ngroups, hg, D).permute(2, 0, 1, 3, 4)
-            vbuf[:, a0 - lo:] = v.transpose(0, 1).reshape(S, B, ngroups, hg, D).permute(2, 0, 1, 3, 4)
+            # [B, S, Hkv, D] -> [ngroups, S, B, hg * D] rows of the buffers
+            for t, buf in ((k, kbuf), (v, vbuf)):
+                _copy_rows(ops, buf[:, a0 - lo:].flatten(3, 4),
+                           t.unflatten(2, (ngroups, hg)).flatten(3, 4).permute(2, 1, 0, 3))
         works = [_fetch(plan, rank, group, (kbuf[g], vbuf[g]), lo) for g in range(ngroups)]
         out = torch.empty_like(q)                        # [B, S, Hq, D]
         lses, probs = [], []
@@ -311,10 +337,16 @@ class _ShardedFunction(torch.autograd.Function):
         ws_bytes = (ops.backward_workspace_bytes(g_q, g_k, spec, kv_len=L)
                     if hasattr(ops, "backward_workspace_bytes") else 0)
         ws_bytes = (ws_bytes + 255) // 256 * 256
-        scratch = _scratch_bytes(kbuf.device, 2 * nkv * 4 + ws_bytes)
+        # the fp32 partials of this rank's rows that higher ranks return: all
+        # groups' receives are in flight together, each group's dK and dV
+        sent_rows = sum(b - a for (_, a, b) in plan.pieces_sent(rank))
+        recv_elems = 2 * sent_rows * kbuf[0, 0].numel()    # per group
+        recv_at = 2 * nkv * 4 + ws_bytes
+        scratch = _scratch_bytes(kbuf.device, recv_at + ngroups * recv_elems * 4)
         dkb = scratch[:nkv * 4].view(torch.float32).view(kbuf.shape)
         dvb = scratch[nkv * 4:2 * nkv * 4].view(torch.float32).view(kbuf.shape)
         ws = scratch[2 * nkv * 4:2 * nkv * 4 + ws_bytes] if ws_bytes else None
+        recv_space = scratch[recv_at:recv_at + ngroups * recv_elems * 4].view(torch.float32)
         pending = []
         for g in range(ngroups):
             h0 = g * hg * G
@@ -336,7 +368,9 @@ class _ShardedFunction(torch.autograd.Function):
                              **({"probs": probs[g]} if probs[g] is not None else {}),
                              **({"workspace": ws} if ws is not None else {}),
                              **({"key_plan": kp} if kp is not None else {}))
-            pending.append(_return_partials(plan, rank, group, (dkb[g], dvb[g]), lo))
+            pending.append(_return_partials(
+                plan, rank, group, (dkb[g], dvb[g]), lo,
+                recv_space[g * recv_elems:(g + 1) * recv_elems]))
         # local rows: own partials plus the fp32 partials returned by higher
         # ranks (only the rows they read, a suffix of this rank's rows)
         dk_loc, dv_loc = dkb[:, a0 - lo:], dvb[:, a0 - lo:]   # [ngroups, S, B, hg, D]
@@ -349,8 +383,8 @@ class _ShardedFunction(torch.autograd.Function):
         with _Span("layout"):
             dk = torch.empty((B, S, ngroups, hg, D), dtype=kbuf.dtype, device=kbuf.device)
             dv = torch.empty_like(dk)
-            dk.copy_(dk_loc.permute(2, 1, 0, 3, 4))
-            dv.copy_(dv_loc.permute(2, 1, 0, 3, 4))
+            for dst, src in ((dk, dk_loc), (dv, dv_loc)):
+                _copy_rows(ops, dst.flatten(3, 4).permute(2, 1, 0, 3), src.flatten(3, 4))
             dk, dv = dk.view(B, S, ngroups * hg, D), dv.view(B, S, ngroups * hg, D)
         return dq, dk, dv, None, None, None, None, None, None, None, None
 

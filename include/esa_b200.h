@@ -287,6 +287,30 @@ int esa_trace_read(int32_t i, const char** name, float* ms);
 int esa_probe_gather(int32_t mode, const esa_problem_t* prob, esa_tensor_t k, esa_tensor_t v,
                      uint32_t* sink, void* stream);
 
+/*
+ * Strided row copy (no reference counterpart: the reference runs on one
+ * device).  The sequence split keeps each KV-head group's K / V rows and its
+ * fp32 partial dK / dV in [rows, B, heads, D] buffers, while its callers hold
+ * [B, S, H, D] tensors; this moves rows between the two layouts on `stream`.
+ * A row is row_elems contiguous elements; row (i0, i1, i2), 0 <= ik <
+ * count[k], starts at element sum ik * src_stride[k] of src and sum ik *
+ * dst_stride[k] of dst.  dtypes: src and dst both BF16 or both F16 (a copy),
+ * or src F32 and dst BF16 / F16 (rounded to nearest even).  row_elems must be
+ * a positive multiple of 8; src, dst and every stride must be 16-byte
+ * aligned.  The rows of dst must not overlap each other or src.
+ */
+typedef struct {
+  const void* src;
+  void* dst;
+  int32_t src_dtype;
+  int32_t dst_dtype;
+  int64_t row_elems;
+  int64_t count[3];
+  int64_t src_stride[3];
+  int64_t dst_stride[3];
+} esa_rows_t;
+int esa_copy_rows(const esa_rows_t* rows, void* stream);
+
 /* Size of the workspace array built into the library for esa_backward_noalloc. */
 #define ESA_NOALLOC_WORKSPACE_BYTES (16u * 1024u * 1024u)
 

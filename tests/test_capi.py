@@ -192,3 +192,63 @@ def test_forward_writes_probs_query(esa, kw, want):
     decision, no GPU needed)."""
     lib = esa._lib.load()
     assert lib.esa_forward_writes_probs(ctypes.byref(_problem(esa, **kw))) == want
+
+
+def test_rows_struct_layout_matches_header(tmp_path, esa):
+    src = tmp_path / "rows.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "esa_b200.h"\n'
+        "int main(void){\n"
+        ' printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(esa_rows_t), offsetof(esa_rows_t, src_dtype),'
+        " offsetof(esa_rows_t, row_elems), offsetof(esa_rows_t, count),"
+        " offsetof(esa_rows_t, src_stride), offsetof(esa_rows_t, dst_stride));\n"
+        " return 0; }\n")
+    exe = tmp_path / "rows"
+    subprocess.run(["gcc", "-std=c99", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)],
+                   check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    R = esa._lib.EsaRows
+    assert got == [ctypes.sizeof(R), R.src_dtype.offset, R.row_elems.offset, R.count.offset,
+                   R.src_stride.offset, R.dst_stride.offset]
+
+
+def _rows(esa, **kw):
+    r = esa._lib.EsaRows()
+    r.src, r.dst, r.src_dtype, r.dst_dtype, r.row_elems = 1 << 20, 1 << 21, 1, 1, 64
+    for i, (n, s, d) in enumerate([(2, 4096, 4096), (3, 256, 256), (4, 64, 64)]):
+        r.count[i], r.src_stride[i], r.dst_stride[i] = n, s, d
+    for key, val in kw.items():
+        if isinstance(val, tuple):
+            getattr(r, key)[val[0]] = val[1]
+        else:
+            setattr(r, key, val)
+    return r
+
+
+@pytest.mark.parametrize("kw,code,frag", [
+    (dict(src_dtype=1, dst_dtype=2), -2, "dtypes"),
+    (dict(src_dtype=2, dst_dtype=0), -2, "dtypes"),
+    (dict(src_dtype=0, dst_dtype=0), -2, "dtypes"),
+    (dict(row_elems=60), -1, "multiple of 8"),
+    (dict(row_elems=0), -1, "multiple of 8"),
+    (dict(src_stride=(1, 260)), -1, "16-byte"),
+    (dict(dst_stride=(2, 4)), -1, "16-byte"),
+    (dict(count=(0, -1)), -1, "negative"),
+    (dict(src=(1 << 20) + 8), -1, "misaligned"),
+    (dict(dst=None), -1, "null"),
+])
+def test_copy_rows_rejects_bad_descriptors(esa, kw, code, frag):
+    """Checked before any CUDA call (no GPU needed)."""
+    lib = esa._lib.load()
+    r = _rows(esa, **kw)
+    assert lib.esa_copy_rows(ctypes.byref(r), None) == code
+    assert frag in lib.esa_last_error().decode()
+
+
+def test_copy_rows_empty_grid_is_a_noop(esa):
+    lib = esa._lib.load()
+    assert lib.esa_copy_rows(ctypes.byref(_rows(esa, count=(1, 0))), None) == 0
+    # fp32 -> bf16 with fp32 strides that are 16-byte multiples (4 elements)
+    r = _rows(esa, src_dtype=0, dst_dtype=1, src_stride=(2, 4), count=(2, 0))
+    assert lib.esa_copy_rows(ctypes.byref(r), None) == 0
