@@ -15,4 +15,4 @@ from .sharded import SequenceShardedElasticSparseAttention
 __all__ = ["ElasticSparseAttention", "ElasticSparseAttentionFunction", "ElasticDecoderStack",
            "HeadShardedElasticSparseAttention", "KeyPlanCache", "PatternSpec",
            "SequenceShardedElasticSparseAttention", "head_share", "layer_ops", "ops", "_lib"]
-__version__ = "0.1.2"
+__version__ = "0.1.3"

@@ -770,7 +770,7 @@ void set_plan(esa::AttnParams& p, const void* plan, const PlanGeom& g) {
 
 extern "C" {
 
-int esa_version(void) { return 120; }
+int esa_version(void) { return 130; }
 
 const char* esa_last_error(void) { return g_last_error.c_str(); }
 

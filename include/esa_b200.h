@@ -151,9 +151,10 @@ typedef struct {
 #define ESA_DEVERR_PLAN 8         /* esa_backward was given a key plan built for
                                      another problem; dk / dv not written */
 
-/* Library version, e.g. 120 for 0.1.2 (110 added head_offset / pattern_heads
+/* Library version, e.g. 130 for 0.1.3 (110 added head_offset / pattern_heads
  * to esa_problem_t, the launch trace and the gather probe; 120 the key plan:
- * key_plan / key_plan_bytes in esa_problem_t, esa_key_plan_size / _build). */
+ * key_plan / key_plan_bytes in esa_problem_t, esa_key_plan_size / _build;
+ * 130 esa_copy_rows). */
 int esa_version(void);
 
 /* Message of the last failing call on this thread ("" if none). */
