@@ -1056,6 +1056,47 @@ def bench_decode(args):
             "clocks": clocks.summary()}
 
 
+def rows_case(args):
+    """The sequence split's two layout copies (esa_copy_rows) at C5's shapes
+    for one of 2 ranks (S = 2^19 rows, 16 KV heads in 4 groups, D = 128):
+    K [B, S, H, D] bf16 -> a [groups, rows, B, 4 x 128] buffer, and fp32
+    partial dK [groups, S, B, 4 x 128] -> bf16 [B, S, H, D].  CUDA-event ms and
+    bandwidth on the bytes each copy must move (median of --steps)."""
+    import elastic_sparse_attention_b200 as esa
+    dev = torch.device("cuda", 0)
+    S, H, ng = C5_L // 2, C5_H, 4
+    hg = H // ng
+    g = torch.Generator(device=dev).manual_seed(0)
+    k = torch.randn(B, S, H, D, device=dev, generator=g, dtype=torch.bfloat16)
+    buf = torch.empty(ng, S, B, hg, D, device=dev, dtype=torch.bfloat16)
+    part = torch.randn(ng, S, B, hg, D, device=dev, generator=g)
+    dk = torch.empty(B, S, ng, hg, D, device=dev, dtype=torch.bfloat16)
+    copies = {
+        "kv_to_buffer": (lambda: esa.ops.copy_rows(
+            buf.flatten(3, 4), k.unflatten(2, (ng, hg)).flatten(3, 4).permute(2, 1, 0, 3)),
+            2 * k.numel() * 2),
+        "partials_to_bf16": (lambda: esa.ops.copy_rows(
+            dk.flatten(3, 4).permute(2, 1, 0, 3), part.flatten(3, 4)), part.numel() * (4 + 2)),
+    }
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {"case": "rows", "shape": f"B={B} S={S} H={H} D={D}, {ng} groups"}
+    for name, (fn, nbytes) in copies.items():
+        times = []
+        for i in range(args.warmup + args.steps):
+            flush.fill_(i & 255)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        out[name] = {"ms": round(ms, 3), "bytes": nbytes, "GBps": round(nbytes / ms / 1e6, 1)}
+    assert torch.equal(dk.flatten(3, 4).permute(2, 1, 0, 3), part.flatten(3, 4).to(torch.bfloat16))
+    print(json.dumps(out))
+
+
 def profile_case(args):
     """One forward + backward of one layer at a reduced C3 shape (for ncu)."""
     import elastic_sparse_attention_b200 as esa
@@ -1087,8 +1128,9 @@ def main():
     ap.add_argument("--c4-seq-len", type=int, default=262144)
     ap.add_argument("--checkpoint", action="store_true",
                     help="c4: recompute each decoder layer in the backward")
-    ap.add_argument("--case", choices=["step", "one-layer"], default="step",
-                    help="one-layer: a single fwd+bwd at --seq-len/--layer, for profilers")
+    ap.add_argument("--case", choices=["step", "one-layer", "rows"], default="step",
+                    help="one-layer: a single fwd+bwd at --seq-len/--layer, for profilers; "
+                         "rows: the sequence split's layout copies at C5's 2-rank shapes")
     ap.add_argument("--seq-len", type=int, default=32768)
     ap.add_argument("--layer", type=int, default=5)
     ap.add_argument("--heads", type=int, default=HQ, help="one-layer: query heads (GQA 4:1)")
@@ -1112,6 +1154,9 @@ def main():
         return
     if args.case == "one-layer":
         profile_case(args)
+        return
+    if args.case == "rows":
+        rows_case(args)
         return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
